@@ -1,0 +1,112 @@
+/*
+ * w4a16_b200.h -- C ABI of the sm_100a (B200) W4A16 fused dequant-GEMM library.
+ *
+ * Plain C: raw device pointers, 64-bit sizes and an opaque stream handle (a
+ * cudaStream_t passed as void*; NULL means the legacy default stream). No
+ * torch or C++ types cross this boundary and no exception escapes it: every
+ * entry point returns 0 on success or a negative W4A16_* status, and
+ * w4a16_strerror() turns a status into text. All launches are asynchronous
+ * on the given stream; nothing here allocates device memory or synchronises.
+ *
+ * Data format (the reference's, unchanged): W is [K, N] (K = in_features),
+ * quantised in groups of G consecutive K-rows per column.
+ *   qweight int32 [K/8, N]  row k = 8i+j of column n in bits [4j, 4j+4) of qweight[i, n]
+ *   scales  fp16  [K/G, N]
+ *   zeros   fp16  [K/G, N]  integer zero-points (0..15 as produced by w4a16_quantize)
+ * All tensors are row-major and dense unless a leading dimension is given.
+ */
+#ifndef W4A16_B200_H_
+#define W4A16_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define W4A16_OK                 0
+#define W4A16_ERR_INVALID       -1  /* bad size, group size or null pointer */
+#define W4A16_ERR_ALIGNMENT     -2  /* pointer/stride alignment a kernel needs is missing */
+#define W4A16_ERR_LAUNCH        -3  /* the CUDA launch itself failed */
+#define W4A16_ERR_DEVICE        -4  /* device is not sm_100 or cannot be queried */
+#define W4A16_ERR_TIMEOUT       -5  /* a kernel's bounded wait expired (sticky device flag) */
+
+/* Input dtypes accepted by w4a16_quantize. */
+#define W4A16_DTYPE_F16  0
+#define W4A16_DTYPE_F32  1
+#define W4A16_DTYPE_BF16 2
+
+/* Library version, major*10000 + minor*100 + patch. */
+int w4a16_version(void);
+
+/* Human-readable text for a status code; never NULL. */
+const char* w4a16_strerror(int status);
+
+/*
+ * Fused GEMM: y[m, n] = sum_k x[m, k] * dequant(qweight, scales, zeros)[k, n]
+ * accumulated in fp32, rounded to fp16, then (if bias != NULL) y + bias[n]
+ * rounded to fp16 again.
+ *
+ * Replaces the reference's w4a16_matmul (w4a16-kernel/src/w4a16/triton_kernel.py:131-200)
+ * and its CUDA twin w4a16_gemm_cuda (w4a16-kernel/src/w4a16/cuda/w4a16_gemm.cu:76-115);
+ * the bias add is the one W4A16Linear.forward does afterwards (linear.py:90-91).
+ *
+ * x: fp16 [M, K] dense. y: fp16, row m at y + m*ldy (ldy >= N), so a caller
+ * can write one column shard of a wider output. Requirements (the reference's
+ * assertions, triton_kernel.py:153-182): K % 8 == 0, K % group_size == 0,
+ * group_size % 64 == 0. M == 0 or N == 0 is a no-op.
+ * Routing: M <= 32 runs the memory-bound decode kernel, larger M the tcgen05
+ * tensor-core kernel (which needs N % 8 == 0; other N fall back to decode
+ * launches over 32-row slices of x).
+ */
+int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales,
+               const void* zeros, const void* bias, void* y,
+               int64_t M, int64_t N, int64_t K, int64_t group_size,
+               int64_t ldy, void* stream);
+
+/*
+ * Group-wise asymmetric uint4 quantisation + packing of w [K, N] (dtype one of
+ * W4A16_DTYPE_*), bit-exact with the reference's quantize_weight
+ * (w4a16-kernel/src/w4a16/quant.py:101-144): fp32 scale (max-min)/15 (1 when
+ * not > 0), zero = clamp(rint(-min/scale), 0, 15), q = clamp(rint(w/scale) + zero, 0, 15).
+ * Requirements: K % 8 == 0, K % group_size == 0, group_size >= 1.
+ * Non-finite weights produce unspecified codes; the caller rejects them first.
+ */
+int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales,
+                   void* zeros, int64_t K, int64_t N, int64_t group_size,
+                   void* stream);
+
+/*
+ * Pack int32 codes q [K, N] (each in 0..15) into qweight [K/8, N]
+ * (w4a16-kernel/src/w4a16/quant.py:45-70). Codes are masked with 0xF; the
+ * range check the reference asserts stays with the caller. K % 8 == 0.
+ */
+int w4a16_pack_int4(const int32_t* q, int32_t* qweight, int64_t K, int64_t N,
+                    void* stream);
+
+/* Inverse of w4a16_pack_int4: qweight [K/8, N] -> q [K, N] in 0..15
+ * (w4a16-kernel/src/w4a16/quant.py:73-95). */
+int w4a16_unpack_int4(const int32_t* qweight, int32_t* q, int64_t K, int64_t N,
+                      void* stream);
+
+/* w[k, n] = fp16(fp16(q - z) * s) for the group of row k, fp16 [K, N]
+ * (w4a16-kernel/src/w4a16/quant.py:147-178). K % group_size == 0, K % 8 == 0. */
+int w4a16_dequantize(const int32_t* qweight, const void* scales, const void* zeros,
+                     void* w, int64_t K, int64_t N, int64_t group_size,
+                     void* stream);
+
+/*
+ * Read and clear the device's sticky error flags for the current device
+ * (bit 0: a pipeline wait in a GEMM kernel ran out of its iteration budget
+ * and the kernel abandoned its tile). Synchronises the given stream.
+ * Returns W4A16_OK when no flag was set, W4A16_ERR_TIMEOUT when one was.
+ * No reference counterpart: the reference's kernels have no bounded waits.
+ */
+int w4a16_check_device_errors(void* stream, uint32_t* flags_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W4A16_B200_H_ */

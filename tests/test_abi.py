@@ -1,0 +1,72 @@
+"""The C-ABI library: it loads without a GPU, exports every symbol the header
+declares, and rejects invalid arguments before touching a device."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from w4a16 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "include", "w4a16_b200.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\**(w4a16_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_builds_and_loads():
+    lib = _lib.lib()
+    assert os.path.exists(_lib.LIB_PATH)
+    assert lib.w4a16_version() >= 10000
+
+
+def test_every_declared_symbol_is_exported():
+    declared = _declared_functions()
+    assert len(declared) >= 8, declared
+    lib = _lib.lib()
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_strerror_covers_every_status():
+    for code in (0, -1, -2, -3, -4, -5):
+        s = _lib.strerror(code)
+        assert s and s != "unknown w4a16 status"
+    assert _lib.strerror(-99) == "unknown w4a16 status"
+
+
+@pytest.mark.parametrize("M,N,K,G,ldy", [
+    (1, 64, 100, 64, 64),      # K % 8
+    (1, 64, 128, 96, 64),      # K % G
+    (1, 64, 128, 32, 64),      # G % 64 (the reference's BLOCK_K rule)
+    (1, 64, 128, 64, 32),      # ldy < N
+    (-1, 64, 128, 64, 64),     # negative M
+])
+def test_gemm_rejects_bad_arguments_without_a_device(M, N, K, G, ldy):
+    lib = _lib.lib()
+    st = lib.w4a16_gemm(None, None, None, None, None, None, M, N, K, G, ldy, None)
+    assert st == -1
+
+
+def test_gemm_empty_is_noop():
+    assert _lib.lib().w4a16_gemm(None, None, None, None, None, None, 0, 64, 128, 64, 64, None) == 0
+
+
+def test_quantize_rejects_bad_arguments_without_a_device():
+    lib = _lib.lib()
+    assert lib.w4a16_quantize(None, 0, None, None, None, 100, 8, 4, None) == -1
+    assert lib.w4a16_quantize(None, 0, None, None, None, 96, 8, 64, None) == -1
+    assert lib.w4a16_pack_int4(None, None, 7, 4, None) == -1
+    assert lib.w4a16_unpack_int4(None, None, 9, 4, None) == -1
+    assert lib.w4a16_dequantize(None, None, None, None, 128, 8, 96, None) == -1
+
+
+def test_check_device_errors_signature():
+    fn = _lib.lib().w4a16_check_device_errors
+    assert fn.argtypes[1] == ctypes.POINTER(ctypes.c_uint32)

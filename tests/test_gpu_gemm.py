@@ -1,0 +1,229 @@
+"""Fused GEMM (decode, prefill and fallback routes) vs the oracle.
+
+Tolerance (tests/tolerance.py): |out - ref| <= 1e-2 + 1e-3*|ref| elementwise
+on the fp16 output, against the reference's fp32-accumulated oracle on the
+same quantised tensors. Ports the reference's test_correctness.py grid and
+error checks, then covers every kernel route and its edges.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import synth
+from helpers import gpu_case, np_, torch_reference
+from tolerance import assert_gemm_close
+from w4a16 import W4A16Linear, quantize_weight, w4a16_matmul
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _oracle_y(X, qw, s, z, G):
+    return oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G)
+
+
+def _build(M, K, N, G, sigma=1.0, seed=0):
+    X, W = gpu_case(M, K, N, G, sigma=sigma, seed=seed)
+    qw, s, z = quantize_weight(W, G)
+    return X, qw, s, z
+
+
+# ---------------------------- golden vectors from the reference --------------------
+def test_golden_cases_match_reference_outputs():
+    g = np.load(os.path.join(GOLDEN, "golden_small.npz"))
+    names = sorted({k.split("/")[0] for k in g.files if not k.startswith("pack_")})
+    for name in names:
+        M, K, N, G = (int(v) for v in g[f"{name}/meta"])
+        if G % 64:
+            continue
+        t = lambda k: torch.from_numpy(g[f"{name}/{k}"]).cuda()  # noqa: E731
+        y = w4a16_matmul(t("X"), t("qweight"), t("scales"), t("zeros"), G)
+        assert_gemm_close(np_(y), g[f"{name}/y_ref"], name)
+
+
+def test_oracle_configuration_output():
+    """16x4096x4096, G=128: the GPU result vs the reference's stored output."""
+    ref = np.load(os.path.join(GOLDEN, "golden_oracle_cfg.npz"))
+    X, W = synth.oracle_cfg_inputs()
+    qw, s, z = quantize_weight(torch.from_numpy(W).cuda(), 128)
+    y = w4a16_matmul(torch.from_numpy(X).cuda(), qw, s, z, 128)
+    assert_gemm_close(np_(y), ref["y_ref"], "oracle configuration")
+
+
+# ---------------------------- the reference's grid (test_correctness.py:35-46) ------
+@pytest.mark.parametrize("M", [1, 16, 64, 256])
+@pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 11008), (11008, 4096)])
+@pytest.mark.parametrize("group_size", [64, 128])
+def test_matches_reference_grid(M, K, N, group_size):
+    X, qw, s, z = _build(M, K, N, group_size)
+    y = w4a16_matmul(X, qw, s, z, group_size)
+    assert y.shape == (M, N) and y.dtype == torch.float16
+    ref = _oracle_y(X, qw, s, z, group_size)
+    assert_gemm_close(np_(y), ref, f"M={M} K={K} N={N} G={group_size}")
+    torch.testing.assert_close(y, torch.from_numpy(ref).cuda(), rtol=1e-2, atol=1e-2)
+
+
+# ---------------------------- every route and its edges ----------------------------
+@pytest.mark.parametrize("M", [1, 2, 7, 8, 9, 15, 16, 17, 24, 25, 31, 32])
+@pytest.mark.parametrize("K,N,G", [(256, 128, 64), (320, 72, 64), (1024, 264, 256), (576, 1000, 192)])
+def test_decode_route(M, K, N, G):
+    X, qw, s, z = _build(M, K, N, G, seed=M * 31 + K)
+    assert_gemm_close(np_(w4a16_matmul(X, qw, s, z, G)), _oracle_y(X, qw, s, z, G), f"decode M={M}")
+
+
+@pytest.mark.parametrize("M", [33, 100, 127, 128, 129, 255, 300])
+@pytest.mark.parametrize("K,N,G", [(64, 8, 64), (320, 264, 64), (1024, 520, 128), (768, 256, 256)])
+def test_prefill_route(M, K, N, G):
+    X, qw, s, z = _build(M, K, N, G, seed=M * 17 + N)
+    assert_gemm_close(np_(w4a16_matmul(X, qw, s, z, G)), _oracle_y(X, qw, s, z, G), f"prefill M={M}")
+
+
+@pytest.mark.parametrize("M", [1, 5, 33, 70])
+@pytest.mark.parametrize("N", [1, 13, 100, 254])
+def test_fallback_route_odd_n(M, N):
+    """N not a multiple of 8 cannot use TMA: the plain-load kernel takes it."""
+    X, qw, s, z = _build(M, 256, N, 64, seed=N)
+    assert_gemm_close(np_(w4a16_matmul(X, qw, s, z, 64)), _oracle_y(X, qw, s, z, 64), f"fallback N={N}")
+
+
+def test_unaligned_views_use_fallback():
+    X, qw, s, z = _build(3, 256, 64, 64)
+    big = torch.zeros(3 * 256 + 8, dtype=torch.float16, device="cuda")
+    Xv = big[4:4 + 3 * 256].view(3, 256)      # 8-byte aligned, not 16
+    Xv.copy_(X)
+    assert Xv.data_ptr() % 16 != 0
+    assert_gemm_close(np_(w4a16_matmul(Xv, qw, s, z, 64)), _oracle_y(X, qw, s, z, 64), "unaligned")
+
+
+def test_empty_and_out_argument():
+    X, qw, s, z = _build(4, 256, 64, 64)
+    y0 = w4a16_matmul(X[:0], qw, s, z, 64)
+    assert y0.shape == (0, 64)
+    out = torch.full((4, 64), 7.0, dtype=torch.float16, device="cuda")
+    y = w4a16_matmul(X, qw, s, z, 64, out=out)
+    assert y.data_ptr() == out.data_ptr()
+    assert_gemm_close(np_(out), _oracle_y(X, qw, s, z, 64), "out=")
+
+
+@pytest.mark.parametrize("M", [1, 20, 200])
+def test_fused_bias_rounds_like_separate_add(M):
+    """Epilogue bias == the reference's separate fp16 ``y + bias`` bit for bit."""
+    X, qw, s, z = _build(M, 512, 264, 128, seed=M)
+    bias = torch.randn(264, device="cuda").half()
+    y = w4a16_matmul(X, qw, s, z, 128)
+    yb = w4a16_matmul(X, qw, s, z, 128, bias=bias)
+    assert torch.equal(yb, y + bias)
+
+
+def test_deterministic():
+    for M in (1, 16, 300):
+        X, qw, s, z = _build(M, 1024, 512, 128, seed=M)
+        a = w4a16_matmul(X, qw, s, z, 128)
+        b = w4a16_matmul(X, qw, s, z, 128)
+        assert torch.equal(a, b)
+
+
+def test_cuda_graph_capture_replays_identically():
+    X, qw, s, z = _build(8, 1024, 512, 128)
+    y = torch.empty(8, 512, dtype=torch.float16, device="cuda")
+    w4a16_matmul(X, qw, s, z, 128, out=y)       # warm-up outside capture
+    torch.cuda.synchronize()
+    ref = y.clone()
+    y.zero_()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        w4a16_matmul(X, qw, s, z, 128, out=y)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)
+
+
+def test_non_default_stream():
+    X, qw, s, z = _build(16, 512, 256, 128)
+    ref = w4a16_matmul(X, qw, s, z, 128)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        y = w4a16_matmul(X, qw, s, z, 128)
+    st.synchronize()
+    assert torch.equal(y, ref)
+
+
+# ---------------------------- error behaviour (test_correctness.py:49-70) -----------
+def test_kernel_asserts_contiguity():
+    X, qw, s, z = _build(8, 128, 64, 64)
+    X_bad = torch.randn(128, 8, dtype=torch.float16, device="cuda").t()
+    assert not X_bad.is_contiguous()
+    with pytest.raises(AssertionError):
+        w4a16_matmul(X_bad, qw, s, z, 64)
+
+
+def test_kernel_rejects_bad_group_size():
+    X, W = gpu_case(8, 64, 64, 8)
+    qw, s, z = quantize_weight(W, 8)
+    with pytest.raises(AssertionError):
+        w4a16_matmul(X, qw, s, z, 8)
+
+
+def test_kernel_rejects_bad_dtypes_and_shapes():
+    X, qw, s, z = _build(2, 128, 64, 64)
+    with pytest.raises(AssertionError):
+        w4a16_matmul(X.float(), qw, s, z, 64)
+    with pytest.raises(AssertionError):
+        w4a16_matmul(X, qw, s[:1], z, 64)
+    with pytest.raises(AssertionError):
+        w4a16_matmul(X[:, :120], qw, s, z, 64)
+
+
+# ---------------------------- module (test_correctness.py:73-89) --------------------
+def test_w4a16_linear_end_to_end():
+    torch.manual_seed(2)
+    K, N, M = 4096, 4096, 16
+    lin = torch.nn.Linear(K, N, bias=True).cuda().half()
+    qlin = W4A16Linear.from_linear(lin, group_size=128)
+    x = torch.randn(M, K, dtype=torch.float16, device="cuda")
+    y = qlin(x)
+    ref = oracle.reference_w4a16(np_(x), np_(qlin.qweight), np_(qlin.scales), np_(qlin.zeros), 128)
+    ref_b = (torch.from_numpy(ref).cuda() + qlin.bias)
+    assert y.shape == (M, N)
+    torch.testing.assert_close(y, ref_b, rtol=1e-2, atol=1e-2)
+    # the module's weights are the reference quantiser's, bit for bit
+    want = oracle.quantize_weight(np_(lin.weight.detach().t().contiguous()), 128)
+    assert np.array_equal(np_(qlin.qweight), want[0])
+
+
+def test_w4a16_linear_3d_input_and_no_bias():
+    lin = torch.nn.Linear(512, 264, bias=False).cuda().half()
+    qlin = W4A16Linear.from_linear(lin, group_size=64)
+    x = torch.randn(2, 3, 512, dtype=torch.float16, device="cuda")
+    y = qlin(x)
+    assert y.shape == (2, 3, 264)
+    ref = _oracle_y(x.reshape(6, 512), qlin.qweight, qlin.scales, qlin.zeros, 64)
+    assert_gemm_close(np_(y.reshape(6, 264)), ref, "3d")
+
+
+def test_w4a16_linear_from_cpu_linear():
+    lin = torch.nn.Linear(256, 64, bias=True).half()
+    qlin = W4A16Linear.from_linear(lin, group_size=128)
+    assert not qlin.qweight.is_cuda
+    qlin = qlin.cuda()
+    x = torch.randn(5, 256, dtype=torch.float16, device="cuda")
+    y = qlin(x)
+    ref = torch.from_numpy(_oracle_y(x, qlin.qweight, qlin.scales, qlin.zeros, 128)).cuda() + qlin.bias
+    assert_gemm_close(np_(y), np_(ref), "cpu-built module")
+
+
+# ---------------------------- cross-route consistency -------------------------------
+def test_decode_and_prefill_routes_agree():
+    """The same rows through the decode route (M <= 32 slices) and the prefill
+    route (all rows at once) agree within the tolerance -- a size-independent
+    property that does not need the oracle."""
+    X, qw, s, z = _build(96, 2048, 768, 128, sigma=0.02)
+    full = w4a16_matmul(X, qw, s, z, 128)
+    parts = torch.cat([w4a16_matmul(X[i:i + 32].contiguous(), qw, s, z, 128) for i in range(0, 96, 32)])
+    assert_gemm_close(np_(parts), np_(full), "decode vs prefill")
+    assert_gemm_close(np_(full), np_(torch_reference(X, qw, s, z, 128)), "vs torch fp32")

@@ -1,0 +1,446 @@
+// w4a16_b200.cu -- the C ABI (include/w4a16_b200.h) over the sm_100a kernels.
+//
+// The library is a single translation unit: the kernels live in the .cuh
+// files included below so that the one sticky device error word has exactly
+// one definition without relocatable device code.
+//
+// Host-side duties: argument validation with the reference's rules
+// (w4a16-kernel/src/w4a16/triton_kernel.py:153-182, quant.py:116-119), the
+// per-device sm_100 check and kernel attributes, TMA tensor-map encoding, the
+// M-bucket routing between the decode and prefill kernels, and turning CUDA
+// launch errors into status codes. Nothing here allocates or synchronises
+// (except w4a16_check_device_errors, which must read the device flag).
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "decode_gemv.cuh"
+#include "prefill_tcgen05.cuh"
+#include "quantize.cuh"
+
+namespace w4a16 {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  static constexpr int kOcc = 64;
+  bool checked = false;
+  bool is_sm100 = false;
+  bool attrs_set = false;
+  int num_sms = 0;
+  int occ_n = 0;
+  long long occ_key[kOcc];
+  int occ_val[kOcc];
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return W4A16_ERR_DEVICE;
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (!d.checked) {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return W4A16_ERR_DEVICE;
+    }
+    d.is_sm100 = (major == 10 && minor == 0);
+    d.num_sms = sms;
+    d.checked = true;
+  }
+  if (!d.is_sm100) return W4A16_ERR_DEVICE;
+  if (!d.attrs_set) {
+    if (cudaFuncSetAttribute(prefill::w4a16_tcgen05_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             prefill::SMEM_BYTES) != cudaSuccess) {
+      cudaGetLastError();
+      return W4A16_ERR_LAUNCH;
+    }
+    auto set_decode = [](auto kern) {
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
+                 cudaSuccess &&
+             cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                 cudaSuccess;
+    };
+    if (!set_decode(decode::decode_gemv_tma_kernel<1>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<2>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<3>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<4>)) {
+      cudaGetLastError();
+      return W4A16_ERR_LAUNCH;
+    }
+    d.attrs_set = true;
+  }
+  *out = &d;
+  return W4A16_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    } else {
+      cudaGetLastError();
+    }
+  }
+  return g_encode;
+}
+
+// 2D row-major tensor map: `cols` contiguous elements per row, `rows` rows,
+// row pitch `ld` elements; box [box_cols x box_rows]; out-of-range boxes
+// read as zero.
+bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t cols,
+                 uint64_t rows, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swz) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * static_cast<uint64_t>(esize)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Resident CTAs per SM of the decode kernel for a token-tile count and a
+// dynamic shared-memory size (cached per device; the set of keys is small).
+int decode_ctas_per_sm(DeviceState& dev, int MT, size_t smem) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < dev.occ_n; ++i) {
+    if (dev.occ_key[i] == static_cast<long long>(MT) * (1ll << 32) + static_cast<long long>(smem))
+      return dev.occ_val[i];
+  }
+  int r = 0;
+  cudaError_t e;
+  switch (MT) {
+    case 1: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<1>, decode::THREADS, smem); break;
+    case 2: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<2>, decode::THREADS, smem); break;
+    case 3: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<3>, decode::THREADS, smem); break;
+    default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<4>, decode::THREADS, smem); break;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (dev.occ_n < DeviceState::kOcc) {
+    dev.occ_key[dev.occ_n] = static_cast<long long>(MT) * (1ll << 32) + static_cast<long long>(smem);
+    dev.occ_val[dev.occ_n] = r;
+    ++dev.occ_n;
+  }
+  return r;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+dim3 grid_2d(int64_t x, int64_t y) {
+  return dim3(static_cast<unsigned>(x), static_cast<unsigned>(y), 1);
+}
+
+// ---------------------------------------------------------------------------
+// GEMM launchers
+// ---------------------------------------------------------------------------
+int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
+                      const __half* z, const __half* bias, __half* y, int M, int N, int K, int G,
+                      long long ldy, cudaStream_t stream) {
+  CUtensorMap tw, ts, tz, tx;
+  const int kstages = (K + decode::KSTAGE - 1) / decode::KSTAGE;
+  if (!make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, qw, N, K / 8, N, decode::BN,
+                   decode::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, N, K / G, N, decode::BN,
+                   decode::SZ_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, z, N, K / G, N, decode::BN,
+                   decode::SZ_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, decode::KSTAGE, M,
+                   CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return W4A16_ERR_ALIGNMENT;
+  }
+  const int chunks = (N + decode::BN - 1) / decode::BN;
+  const int MT = (M + 7) / 8;
+  const int sbytes = decode::stage_bytes(M);
+  // Ring depth: ~100 KB of stages (>= 2, <= 8) so two CTAs fit on an SM.
+  int nst = (100 * 1024 - decode::red_bytes(MT)) / sbytes;
+  nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
+  auto smem_for = [&](int stages) {
+    return 1024 + static_cast<size_t>(stages) * sbytes + decode::red_bytes(MT) +
+           2 * stages * sizeof(uint64_t);
+  };
+  const int resident = decode_ctas_per_sm(dev, MT, smem_for(nst));
+  if (resident <= 0) return W4A16_ERR_LAUNCH;
+  const int capacity = resident * dev.num_sms;
+  // Split K over a cluster while the grid still fits in one resident wave and
+  // each CTA keeps >= 2 stages. Cluster sizes divide the strip (1, 2, 4, 8).
+  int split = 1;
+  while (split < 8 && chunks * split * 2 <= capacity && kstages >= split * 4) split *= 2;
+  const int per_cta = (kstages + split - 1) / split;
+  if (nst > per_cta) nst = per_cta < 2 ? 2 : per_cta;
+  const size_t smem = smem_for(nst);
+
+  decode::Params p;
+  p.bias = bias;
+  p.y = y;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.G = G;
+  p.ldy = ldy;
+  p.stages_per_cta = per_cta;
+  p.num_stages = nst;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid_2d(chunks, split);
+  cfg.blockDim = dim3(decode::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = split;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+  switch (MT) {
+    case 1: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1>, tw, ts, tz, tx, p); break;
+    case 2: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2>, tw, ts, tz, tx, p); break;
+    case 3: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<3>, tw, ts, tz, tx, p); break;
+    default: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<4>, tw, ts, tz, tx, p); break;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_LAUNCH;
+  }
+  return W4A16_OK;
+}
+
+int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, const __half* z,
+                           const __half* bias, __half* y, int64_t M, int N, int K, int G,
+                           long long ldy, cudaStream_t stream) {
+  for (int64_t m0 = 0; m0 < M; m0 += 32) {
+    const int mc = static_cast<int>(M - m0 < 32 ? M - m0 : 32);
+    decode::decode_gemv_fallback_kernel<<<grid_2d((N + decode::FB_THREADS - 1) / decode::FB_THREADS, 1),
+                                          decode::FB_THREADS, 0, stream>>>(
+        x + m0 * K, qw, s, z, bias, y + m0 * ldy, mc, N, K, G, ldy);
+    W4A16_RETURN_IF_LAUNCH_FAILED();
+  }
+  return W4A16_OK;
+}
+
+int launch_prefill(const __half* x, const int32_t* qw, const __half* s, const __half* z,
+                   const __half* bias, __half* y, int M, int N, int K, int G, long long ldy,
+                   cudaStream_t stream) {
+  CUtensorMap tx, tp, ts, tz;
+  if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tp, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, qw, N, K / 8, N, prefill::BN,
+                   prefill::BK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, N, K / G, N, prefill::BN, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, z, N, K / G, N, prefill::BN, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return W4A16_ERR_ALIGNMENT;
+  }
+  prefill::Params p;
+  p.bias = bias;
+  p.y = y;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.G = G;
+  p.ldy = ldy;
+  p.vec_store = (aligned16(y) && (ldy % 8) == 0) ? 1 : 0;
+  const dim3 grid = grid_2d((M + prefill::BM - 1) / prefill::BM, (N + prefill::BN - 1) / prefill::BN);
+  prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, tp, ts,
+                                                                                       tz, p);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
+}
+
+}  // namespace
+}  // namespace w4a16
+
+using namespace w4a16;
+
+extern "C" {
+
+int w4a16_version(void) { return 10000; }
+
+const char* w4a16_strerror(int status) {
+  switch (status) {
+    case W4A16_OK: return "ok";
+    case W4A16_ERR_INVALID: return "invalid argument (size, group size or null pointer)";
+    case W4A16_ERR_ALIGNMENT: return "pointer or stride alignment not supported";
+    case W4A16_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case W4A16_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) GPU";
+    case W4A16_ERR_TIMEOUT: return "a kernel's bounded pipeline wait expired (device error flag set)";
+    default: return "unknown w4a16 status";
+  }
+}
+
+int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+               const void* bias, void* y, int64_t M, int64_t N, int64_t K, int64_t group_size,
+               int64_t ldy, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
+  if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
+  if (ldy < N) return W4A16_ERR_INVALID;
+  if (M == 0 || N == 0) return W4A16_OK;
+  if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || y == nullptr)
+    return W4A16_ERR_INVALID;
+  if (N > (1ll << 30) || K > (1ll << 30) || M > (1ll << 31) - 1) return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* sh = static_cast<const __half*>(scales);
+  const __half* zh = static_cast<const __half*>(zeros);
+  const __half* bh = static_cast<const __half*>(bias);
+  __half* yh = static_cast<__half*>(y);
+  const bool tma_ok = (N % 8 == 0) && aligned16(x) && aligned16(qweight) && aligned16(scales) &&
+                      aligned16(zeros);
+  const int n = static_cast<int>(N), k = static_cast<int>(K), g = static_cast<int>(group_size);
+  if (!tma_ok) {
+    return launch_decode_fallback(xh, qweight, sh, zh, bh, yh, M, n, k, g, ldy, s);
+  }
+  if (M <= 32) {
+    return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy, s);
+  }
+  return launch_prefill(xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy, s);
+}
+
+int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,
+                   int64_t K, int64_t N, int64_t group_size, void* stream) {
+  if (K < 0 || N < 0 || group_size <= 0) return W4A16_ERR_INVALID;
+  if (K % 8 != 0 || K % group_size != 0) return W4A16_ERR_INVALID;
+  if (K == 0 || N == 0) return W4A16_OK;
+  if (w == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr)
+    return W4A16_ERR_INVALID;
+  if (K / group_size > 65535 || K / 8 > 65535) return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid = grid_2d((N + 255) / 256, K / group_size);
+  __half* sh = static_cast<__half*>(scales);
+  __half* zh = static_cast<__half*>(zeros);
+  switch (w_dtype) {
+    case W4A16_DTYPE_F16:
+      quantize_pack_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(w), qweight, sh,
+                                                         zh, N, group_size);
+      break;
+    case W4A16_DTYPE_F32:
+      quantize_pack_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(w), qweight, sh,
+                                                        zh, N, group_size);
+      break;
+    case W4A16_DTYPE_BF16:
+      quantize_pack_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(w), qweight, sh, zh, N, group_size);
+      break;
+    default:
+      return W4A16_ERR_INVALID;
+  }
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  if (group_size % 8 != 0) {
+    const dim3 pg = grid_2d((N + 255) / 256, K / 8);
+    switch (w_dtype) {
+      case W4A16_DTYPE_F16:
+        pack_ragged_groups_kernel<__half><<<pg, 256, 0, s>>>(static_cast<const __half*>(w), qweight,
+                                                              N, K, group_size);
+        break;
+      case W4A16_DTYPE_F32:
+        pack_ragged_groups_kernel<float><<<pg, 256, 0, s>>>(static_cast<const float*>(w), qweight,
+                                                             N, K, group_size);
+        break;
+      default:
+        pack_ragged_groups_kernel<__nv_bfloat16><<<pg, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(w), qweight, N, K, group_size);
+        break;
+    }
+    W4A16_RETURN_IF_LAUNCH_FAILED();
+  }
+  return W4A16_OK;
+}
+
+int w4a16_pack_int4(const int32_t* q, int32_t* qweight, int64_t K, int64_t N, void* stream) {
+  if (K < 0 || N < 0 || K % 8 != 0) return W4A16_ERR_INVALID;
+  if (K == 0 || N == 0) return W4A16_OK;
+  if (q == nullptr || qweight == nullptr || K / 8 > 65535) return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  pack_int4_kernel<<<grid_2d((N + 255) / 256, K / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, qweight, N);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
+}
+
+int w4a16_unpack_int4(const int32_t* qweight, int32_t* q, int64_t K, int64_t N, void* stream) {
+  if (K < 0 || N < 0 || K % 8 != 0) return W4A16_ERR_INVALID;
+  if (K == 0 || N == 0) return W4A16_OK;
+  if (q == nullptr || qweight == nullptr || K / 8 > 65535) return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  unpack_int4_kernel<<<grid_2d((N + 255) / 256, K / 8), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(qweight, q, N);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
+}
+
+int w4a16_dequantize(const int32_t* qweight, const void* scales, const void* zeros, void* w,
+                     int64_t K, int64_t N, int64_t group_size, void* stream) {
+  if (K < 0 || N < 0 || group_size <= 0 || K % 8 != 0 || K % group_size != 0)
+    return W4A16_ERR_INVALID;
+  if (K == 0 || N == 0) return W4A16_OK;
+  if (qweight == nullptr || scales == nullptr || zeros == nullptr || w == nullptr ||
+      K / 8 > 65535)
+    return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  dequantize_kernel<<<grid_2d((N + 255) / 256, K / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      qweight, static_cast<const __half*>(scales), static_cast<const __half*>(zeros),
+      static_cast<__half*>(w), N, group_size);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
+}
+
+int w4a16_check_device_errors(void* stream, uint32_t* flags_out) {
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t flags = 0;
+  const uint32_t zero = 0;
+  if (cudaMemcpyFromSymbolAsync(&flags, g_device_error, sizeof(flags), 0,
+                                cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice,
+                              s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_LAUNCH;
+  }
+  if (flags_out != nullptr) *flags_out = flags;
+  return flags == 0 ? W4A16_OK : W4A16_ERR_TIMEOUT;
+}
+
+}  // extern "C"

@@ -1,0 +1,100 @@
+"""ctypes binding of the sm_100a C-ABI library (``include/w4a16_b200.h``).
+
+The shared library is built in-tree by ``build.py`` (or ``__graft_entry__.build()``)
+next to this file. Loading it needs no GPU; calling into it needs a B200
+(sm_100). There is no CPU fallback: if the library is missing, every GEMM /
+quantisation entry point raises ``RuntimeError`` naming the missing file.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libw4a16_b200.so")
+
+W4A16_OK = 0
+W4A16_ERR_TIMEOUT = -5
+DTYPE_CODES = {torch.float16: 0, torch.float32: 1, torch.bfloat16: 2}
+
+# Every symbol the header declares, with its ctypes signature.
+_c_i64 = ctypes.c_int64
+_vp = ctypes.c_void_p
+SIGNATURES = {
+    "w4a16_version": ([], ctypes.c_int),
+    "w4a16_strerror": ([ctypes.c_int], ctypes.c_char_p),
+    "w4a16_gemm": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp],
+                   ctypes.c_int),
+    "w4a16_quantize": ([_vp, ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
+    "w4a16_pack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
+    "w4a16_unpack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
+    "w4a16_dequantize": ([_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
+    "w4a16_check_device_errors": ([_vp, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class W4A16Error(RuntimeError):
+    """A non-zero status returned by the C ABI."""
+
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what} failed: {strerror(status)} (status {status})")
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library; raise loudly if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"W4A16 sm_100a library not built: {LIB_PATH} is missing. Build it with "
+                    "`python w4a16-dequant-fused-matmul-kernel_b200/build.py` (there is no CPU "
+                    "or PyTorch fallback for the W4A16 kernels).")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (argtypes, restype) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.argtypes = argtypes
+                fn.restype = restype
+            _lib = handle
+    return _lib
+
+
+def strerror(status: int) -> str:
+    return lib().w4a16_strerror(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != W4A16_OK:
+        raise W4A16Error(status, what)
+
+
+def stream_of(device: torch.device) -> int:
+    """Raw cudaStream_t of torch's current stream on ``device``."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def check_device_errors(device: torch.device | int | None = None) -> int:
+    """Read and clear the device's sticky kernel error flags (synchronises).
+
+    Raises :class:`W4A16Error` if a GEMM kernel's bounded wait expired since
+    the last check; returns 0 otherwise.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(
+        "cuda", device) if isinstance(device, int) else device
+    flags = ctypes.c_uint32(0)
+    with torch.cuda.device(dev):
+        st = lib().w4a16_check_device_errors(stream_of(dev), ctypes.byref(flags))
+    check(st, "w4a16_check_device_errors")
+    return int(flags.value)

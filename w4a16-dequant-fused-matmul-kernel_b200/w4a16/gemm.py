@@ -1,0 +1,125 @@
+"""``w4a16_matmul`` -- the fused W4A16 GEMM on B200 (sm_100a).
+
+Drop-in for the reference's ``w4a16_matmul`` (w4a16-kernel/src/w4a16/triton_kernel.py:131-200):
+same signature, same argument meaning, same ``AssertionError`` conditions and
+messages, same fresh-or-``out`` output contract. The work runs in the
+hand-written sm_100a library through its C ABI, on torch's current stream:
+
+* ``M <= 32``  -> the memory-bound decode kernel (TMA-fed, tensor-core MMA on
+  register-dequantised fragments, cluster split-K);
+* ``M > 32``   -> the tcgen05/TMEM prefill kernel (128x256 tiles).
+
+Group sizes: the reference requires every autotune ``BLOCK_K`` (32 and 64) to
+divide ``group_size`` (triton_kernel.py:177-182), i.e. ``group_size % 64 == 0``;
+the same rule holds here and raises the same ``AssertionError``.
+
+Zero-points must be integers in ``[0, 15]`` as ``quantize_weight`` produces
+them (the format's contract); the kernels subtract them exactly through the
+fp16 magic-number trick, which relies on it.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+__all__ = ["w4a16_matmul"]
+
+# The reference's smallest and largest BLOCK_K; every group size must be a multiple of both.
+_BLOCK_K_RULE = 64
+
+
+def w4a16_matmul(
+    x: Tensor,
+    qweight: Tensor,
+    scales: Tensor,
+    zeros: Tensor,
+    group_size: int,
+    out: Tensor | None = None,
+    *,
+    bias: Tensor | None = None,
+) -> Tensor:
+    """Fused W4A16 GEMM: ``Y = X @ dequant(qweight)`` (fp32 accumulate, fp16 out).
+
+    Args:
+        x: activations [M, K] fp16, contiguous, on CUDA.
+        qweight: int32 [K//8, N], contiguous, on CUDA.
+        scales: fp16 [K//G, N], contiguous, on CUDA.
+        zeros: fp16 [K//G, N], contiguous, on CUDA.
+        group_size: G. Must satisfy G | K, 8 | K and 64 | G.
+        out: optional preallocated fp16 [M, N] output.
+        bias: optional fp16 [N] (extension): the result is ``fp16(Y) + bias``
+            rounded to fp16, fused into the kernel's epilogue.
+
+    Returns:
+        fp16 tensor [M, N].
+    """
+    assert x.is_cuda, "x must be on CUDA (a B200 / sm_100 device)"
+    assert qweight.is_cuda and scales.is_cuda and zeros.is_cuda, "all inputs must be on CUDA"
+    assert x.dtype == torch.float16, f"x must be fp16, got {x.dtype}"
+    assert qweight.dtype == torch.int32, f"qweight must be int32, got {qweight.dtype}"
+    assert scales.dtype == torch.float16, f"scales must be fp16, got {scales.dtype}"
+    assert zeros.dtype == torch.float16, f"zeros must be fp16, got {zeros.dtype}"
+    assert x.dim() == 2 and qweight.dim() == 2, "x and qweight must be 2D"
+
+    M, K = x.shape
+    Kp, N = qweight.shape
+    assert Kp * 8 == K, f"qweight rows (K//8)={Kp} incompatible with x K={K}"
+    assert K % 8 == 0, f"K={K} must be divisible by 8"
+    assert K % group_size == 0, f"K={K} must be divisible by group_size={group_size}"
+    num_groups = K // group_size
+    assert scales.shape == (num_groups, N), f"scales shape {tuple(scales.shape)} != {(num_groups, N)}"
+    assert zeros.shape == (num_groups, N), f"zeros shape {tuple(zeros.shape)} != {(num_groups, N)}"
+
+    assert x.is_contiguous(), "x must be contiguous"
+    assert qweight.is_contiguous(), "qweight must be contiguous"
+    assert scales.is_contiguous(), "scales must be contiguous"
+    assert zeros.is_contiguous(), "zeros must be contiguous"
+
+    assert group_size % _BLOCK_K_RULE == 0, (
+        f"group_size={group_size} must be a multiple of {_BLOCK_K_RULE} (every K tile of the "
+        f"kernels must lie inside one quantisation group)"
+    )
+    dev = x.device
+    assert qweight.device == dev and scales.device == dev and zeros.device == dev, (
+        "all inputs must be on the same CUDA device"
+    )
+    if bias is not None:
+        assert bias.is_cuda and bias.device == dev, "bias must be on the inputs' CUDA device"
+        assert bias.dtype == torch.float16 and bias.shape == (N,) and bias.is_contiguous(), (
+            f"bias must be a contiguous fp16 [{N}] tensor"
+        )
+
+    if out is None:
+        y = torch.empty((M, N), device=dev, dtype=torch.float16)
+    else:
+        assert out.shape == (M, N) and out.dtype == torch.float16 and out.is_contiguous()
+        assert out.device == dev, "out must be on the inputs' CUDA device"
+        y = out
+
+    lib = _lib.lib()
+    with torch.cuda.device(dev):
+        st = lib.w4a16_gemm(
+            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+            _lib.ptr(bias), y.data_ptr(), M, N, K, group_size, N, _lib.stream_of(dev))
+    _lib.check(st, "w4a16_gemm")
+    return y
+
+
+def w4a16_matmul_into(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
+                      y: Tensor, ldy: int, bias: Tensor | None = None) -> None:
+    """Low-level variant: write ``Y`` into rows of pitch ``ldy`` starting at
+    ``y``'s first element (e.g. one column shard of a wider output buffer).
+
+    No shape assertions beyond what the C ABI checks; used by the sharded
+    layers in :mod:`w4a16.parallel`.
+    """
+    M, K = x.shape
+    N = qweight.shape[1]
+    dev = x.device
+    with torch.cuda.device(dev):
+        st = _lib.lib().w4a16_gemm(
+            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+            _lib.ptr(bias), y.data_ptr(), M, N, K, group_size, ldy, _lib.stream_of(dev))
+    _lib.check(st, "w4a16_gemm")
