@@ -58,13 +58,23 @@ struct Params {
 };
 
 // Dequantise one packed word (8 consecutive K of one column) into 8 fp16 in
-// natural K order: pairs (k0,k1) (k2,k3) (k4,k5) (k6,k7). zc = (1024+z, 64+z).
+// natural K order: pairs (k0,k1) (k2,k3) (k4,k5) (k6,k7). Byte b of the word
+// holds nibbles (2b, 2b+1); PRMT copies it into bytes 0 and 2, then one LOP3
+// keeps the low nibble in the low half (as fp16 1024 + n, magic 0x6400) and
+// the high nibble of the copy in the high half (as fp16 64 + n, magic 0x5400,
+// nibble at mantissa bits 4-7). zc = (1024+z, 64+z) makes the subtraction exact.
+__device__ __forceinline__ uint32_t dequant_byte_pair(uint32_t w, uint32_t sel, uint32_t zc,
+                                                      uint32_t ss) {
+  const uint32_t t = lop3_and_or(prmt(w, 0u, sel), 0x00F0000Fu, 0x54006400u);
+  return hmul2_u32(hsub2_u32(t, zc), ss);
+}
+
 __device__ __forceinline__ uint4 dequant_word_nat(uint32_t w, uint32_t zc, uint32_t ss) {
   uint4 r;
-  r.x = hmul2_u32(hsub2_u32(lop3_and_or(w, 0x00F0000Fu, 0x54006400u), zc), ss);
-  r.y = hmul2_u32(hsub2_u32(lop3_and_or(w >> 8, 0x00F0000Fu, 0x54006400u), zc), ss);
-  r.z = hmul2_u32(hsub2_u32(lop3_and_or(w >> 16, 0x00F0000Fu, 0x54006400u), zc), ss);
-  r.w = hmul2_u32(hsub2_u32(lop3_and_or(w >> 24, 0x00F0000Fu, 0x54006400u), zc), ss);
+  r.x = dequant_byte_pair(w, 0x4040u, zc, ss);
+  r.y = dequant_byte_pair(w, 0x4141u, zc, ss);
+  r.z = dequant_byte_pair(w, 0x4242u, zc, ss);
+  r.w = dequant_byte_pair(w, 0x4343u, zc, ss);
   return r;
 }
 
