@@ -6,7 +6,8 @@
  * torch or C++ types cross this boundary and no exception escapes it: every
  * entry point returns 0 on success or a negative W4A16_* status, and
  * w4a16_strerror() turns a status into text. All launches are asynchronous
- * on the given stream; nothing here allocates device memory or synchronises.
+ * on the given stream; nothing here allocates device memory or synchronises
+ * (scratch memory, where a kernel needs it, is passed in by the caller).
  *
  * Data format (the reference's, unchanged): W is [K, N] (K = in_features),
  * quantised in groups of G consecutive K-rows per column.
@@ -31,6 +32,7 @@ extern "C" {
 #define W4A16_ERR_LAUNCH        -3  /* the CUDA launch itself failed */
 #define W4A16_ERR_DEVICE        -4  /* device is not sm_100 or cannot be queried */
 #define W4A16_ERR_TIMEOUT       -5  /* a kernel's bounded wait expired (sticky device flag) */
+#define W4A16_ERR_WORKSPACE     -6  /* workspace missing, too small or misaligned */
 
 /* Input dtypes accepted by w4a16_quantize. */
 #define W4A16_DTYPE_F16  0
@@ -59,11 +61,28 @@ const char* w4a16_strerror(int status);
  * Routing: M <= 32 runs the memory-bound decode kernel, larger M the tcgen05
  * tensor-core kernel (which needs N % 8 == 0; other N fall back to decode
  * launches over 32-row slices of x).
+ *
+ * workspace: device scratch of at least w4a16_gemm_workspace_size() bytes,
+ * 256-byte aligned, ZEROED before its first use. The decode kernel keeps
+ * per-strip arrival counters and partial sums there and leaves the counters
+ * zero again when it completes, so one zeroed buffer serves every later call
+ * on the same stream; launches that may run concurrently need separate
+ * workspaces. (A launch abandoned on W4A16_ERR_TIMEOUT can leave counters
+ * set: zero the buffer again before reusing it.) May be NULL when the size
+ * query returned 0.
  */
 int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales,
                const void* zeros, const void* bias, void* y,
                int64_t M, int64_t N, int64_t K, int64_t group_size,
-               int64_t ldy, void* stream);
+               int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Bytes of workspace w4a16_gemm needs for this shape on the current device
+ * (0 for shapes whose kernels need none). No reference counterpart: the
+ * reference's kernels never split K across thread blocks.
+ */
+int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_size,
+                              int64_t* bytes_out);
 
 /*
  * Group-wise asymmetric uint4 quantisation + packing of w [K, N] (dtype one of

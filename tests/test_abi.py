@@ -34,8 +34,17 @@ def test_every_declared_symbol_is_exported():
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def test_workspace_size_query_without_a_device():
+    out = ctypes.c_int64(-1)
+    lib = _lib.lib()
+    assert lib.w4a16_gemm_workspace_size(1, 64, 100, 64, ctypes.byref(out)) == -1
+    # routes that need no workspace answer without touching a device
+    assert lib.w4a16_gemm_workspace_size(64, 256, 256, 64, ctypes.byref(out)) == 0 and out.value == 0
+    assert lib.w4a16_gemm_workspace_size(4, 13, 256, 64, ctypes.byref(out)) == 0 and out.value == 0
+
+
 def test_strerror_covers_every_status():
-    for code in (0, -1, -2, -3, -4, -5):
+    for code in (0, -1, -2, -3, -4, -5, -6):
         s = _lib.strerror(code)
         assert s and s != "unknown w4a16 status"
     assert _lib.strerror(-99) == "unknown w4a16 status"
@@ -50,12 +59,12 @@ def test_strerror_covers_every_status():
 ])
 def test_gemm_rejects_bad_arguments_without_a_device(M, N, K, G, ldy):
     lib = _lib.lib()
-    st = lib.w4a16_gemm(None, None, None, None, None, None, M, N, K, G, ldy, None)
+    st = lib.w4a16_gemm(None, None, None, None, None, None, M, N, K, G, ldy, None, 0, None)
     assert st == -1
 
 
 def test_gemm_empty_is_noop():
-    assert _lib.lib().w4a16_gemm(None, None, None, None, None, None, 0, 64, 128, 64, 64, None) == 0
+    assert _lib.lib().w4a16_gemm(None, None, None, None, None, None, 0, 64, 128, 64, 64, None, 0, None) == 0
 
 
 def test_quantize_rejects_bad_arguments_without_a_device():

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -97,26 +98,30 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// try_wait suspends the thread until the phase completes or the hinted time
+// (ns) passes, so a waiting warp issues almost nothing while it waits.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
 
 // Wait until the phase with the given parity has completed. Returns false (and
-// raises the sticky error bit) when the budget runs out.
+// raises the sticky error bit) when the time budget runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) break;
+    if ((i & 7u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) break;
   }
   flag_error(kErrWaitTimeout);
   return false;

@@ -2,27 +2,33 @@
 // on the 5th-generation tensor cores (tcgen05, accumulators in TMEM).
 //
 // Replaces the reference's Triton kernel (w4a16-kernel/src/w4a16/triton_kernel.py:62-128)
-// for large M. One CTA computes a 128 x 256 tile of y; the K loop runs in
-// 64-wide steps through a 3-deep shared-memory ring:
+// for large M. Persistent CTAs (one per SM) walk 128 x 256 output tiles; the
+// K loop of a tile runs in 64-wide steps. Warp roles:
 //
-//   warp 0      TMA producer: x tile [128 x 64] fp16 (128-byte swizzle),
-//               packed qweight tile [8 x 256] int32, and the step's scale and
-//               zero rows [256] fp16, all on one transaction-counted mbarrier.
-//   warps 2..9  dequantisers: thread t owns column t of the tile, unpacks its 8
-//               words (magic-number nibble extraction, exact (q - z), one fp16
-//               multiply by s: the reference's rounding) and writes the fp16
-//               weights K-major into the 128-byte-swizzled B tile, then
-//               fence.proxy.async + arrive so the tensor core may read them.
-//   warp 1      TMEM allocator + single-thread MMA issuer:
-//               tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16, four per
-//               step, fp32 accumulator in 256 TMEM columns; tcgen05.commit
-//               frees the ring slot.
-//   epilogue    warps 2..9 read the accumulator with tcgen05.ld (each warp its
-//               32-lane TMEM quarter, 128 columns), round to fp16, add the
-//               optional bias (rounded again, as W4A16Linear does) and store.
+//   warp 0       TMA producer: per step the x tile [128 x 64] fp16 (128-byte
+//                swizzle), the packed qweight tile [8 x 256] int32 and the
+//                step's scale and zero rows [256] fp16 into a 6-deep ring, all
+//                on one transaction-counted mbarrier.
+//   warps 2..9   dequantisers: thread t owns column t of the tile; it unpacks
+//                the column's 8 words of the step (PRMT + LOP3 magic-number
+//                nibble extraction, exact (q - z), one fp16 multiply by s: the
+//                reference's rounding) and writes the fp16 weights K-major into
+//                a 128-byte-swizzled B tile of a 2-deep ring, then
+//                fence.proxy.async so the tensor core may read them.
+//   warp 1       TMEM allocator (512 columns: two 256-column fp32
+//                accumulators) and single-thread MMA issuer:
+//                tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16, four per
+//                step; tcgen05.commit frees the ring slots and, after a tile's
+//                last step, hands its accumulator to the epilogue.
+//   warps 10..13 epilogue: each warp reads its 32-lane TMEM quarter with
+//                tcgen05.ld, rounds to fp16, adds the optional bias (rounded
+//                again, as W4A16Linear's separate add does) and stores; the
+//                double-buffered accumulator lets this overlap the next tile's
+//                main loop.
 //
-// Every mbarrier wait is bounded; on expiry the CTA raises the sticky device
-// error bit, drains its in-flight copies, frees its TMEM and exits.
+// Every mbarrier wait is bounded; on expiry the role raises the sticky device
+// error bit and leaves its loops, the producer drains its in-flight copies,
+// the MMA issuer waits for its last MMAs, and TMEM is freed before exit.
 #pragma once
 
 #include "common.cuh"
@@ -33,27 +39,34 @@ namespace prefill {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int STAGES = 3;
-constexpr int A_BYTES = BM * BK * 2;        // 16384
-constexpr int B_BYTES = BN * BK * 2;        // 32768
-constexpr int P_BYTES = (BK / 8) * BN * 4;  // 8192
-constexpr int SZ_BYTES = BN * 2;            // 512
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES + 2 * SZ_BYTES;  // 58368 = 57 KiB
-constexpr int TX_BYTES = A_BYTES + P_BYTES + 2 * SZ_BYTES;               // via TMA
-constexpr int NUM_WARPS = 10;
+constexpr int TSTAGES = 6;                   // TMA ring depth
+constexpr int BSTAGES = 2;                   // dequantised-B ring depth
+constexpr int A_BYTES = BM * BK * 2;         // 16384
+constexpr int P_BYTES = (BK / 8) * BN * 4;   // 8192
+constexpr int SZ_BYTES = BN * 2;             // 512
+constexpr int T_BYTES = A_BYTES + P_BYTES + 2 * SZ_BYTES;   // 25600 = 25 KiB per TMA stage
+constexpr int B_BYTES = BN * BK * 2;         // 32768
+constexpr int DQ_WARPS = 8;
+constexpr int EPI_WARPS = 4;
+constexpr int NUM_WARPS = 2 + DQ_WARPS + EPI_WARPS;
 constexpr int THREADS = NUM_WARPS * 32;
-constexpr int DQ_THREADS = 256;
-constexpr uint32_t TMEM_COLS = 256;
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+constexpr int EPI_WARP0 = 2 + DQ_WARPS;
+constexpr uint32_t ACC_COLS = 256;
+constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+constexpr int BAR_BYTES = 256;
+constexpr int SMEM_BYTES = 1024 + TSTAGES * T_BYTES + BSTAGES * B_BYTES + BAR_BYTES;
 constexpr uint32_t IDESC = umma_idesc_f16_f32(BM, BN);
 
-static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment");
+static_assert(T_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 struct Params {
   const __half* bias;
   __half* y;
   int M, N, K, G;
+  int g_shift;     // log2(G) when G is a power of two, else -1
   long long ldy;
+  int m_tiles, n_tiles;
   int vec_store;   // y and ldy allow 16-byte stores
 };
 
@@ -78,6 +91,23 @@ __device__ __forceinline__ uint4 dequant_word_nat(uint32_t w, uint32_t zc, uint3
   return r;
 }
 
+// Lane 0 waits, the warp follows: keeps mbarrier polling off the shared-memory pipe.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  __syncwarp();
+  return ok;
+}
+
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void advance(int depth) {
+    if (++slot == depth) { slot = 0; phase ^= 1u; }
+  }
+};
+
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x,
                          const __grid_constant__ CUtensorMap tm_p,
@@ -86,25 +116,37 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* bfull = full + STAGES;
-  uint64_t* empty = bfull + STAGES;
-  uint64_t* accfull = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
+  uint8_t* tring = smem;                                   // TSTAGES x {A, P, S, Z}
+  uint8_t* bring = smem + TSTAGES * T_BYTES;               // BSTAGES x B
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + BSTAGES * B_BYTES);
+  uint64_t* tfull = bars;
+  uint64_t* tempty = tfull + TSTAGES;
+  uint64_t* bfull = tempty + TSTAGES;
+  uint64_t* bempty = bfull + BSTAGES;
+  uint64_t* accfull = bempty + BSTAGES;
+  uint64_t* accempty = accfull + 2;
+  uint64_t* drain = accempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM;
-  const int n0 = blockIdx.y * BN;
   const int KT = p.K / BK;
+  const int ntiles = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&bfull[s], DQ_THREADS);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < TSTAGES; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 1);
     }
-    mbar_init(accfull, 1);
+    for (int j = 0; j < BSTAGES; ++j) {
+      mbar_init(&bfull[j], DQ_WARPS);
+      mbar_init(&bempty[j], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accfull[a], 1);
+      mbar_init(&accempty[a], EPI_WARPS);
+    }
+    mbar_init(drain, 1);
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -121,87 +163,122 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
       tma_prefetch_desc(&tm_p);
-      int issued = 0;
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES) {
-          if (!mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) break;
+      tma_prefetch_desc(&tm_s);
+      tma_prefetch_desc(&tm_z);
+      Ring r;
+      long long issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        const int m0 = (tile % p.m_tiles) * BM;
+        const int n0 = (tile / p.m_tiles) * BN;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u)) { ok = false; break; }
+          uint8_t* st = tring + r.slot * T_BYTES;
+          const int kk = kt * BK;
+          const int grow = p.g_shift >= 0 ? kk >> p.g_shift : kk / p.G;
+          mbar_arrive_expect_tx(&tfull[r.slot], T_BYTES);
+          tma_load_2d(st, &tm_x, &tfull[r.slot], kk, m0);
+          tma_load_2d(st + A_BYTES, &tm_p, &tfull[r.slot], n0, kt * (BK / 8));
+          tma_load_2d(st + A_BYTES + P_BYTES, &tm_s, &tfull[r.slot], n0, grow);
+          tma_load_2d(st + A_BYTES + P_BYTES + SZ_BYTES, &tm_z, &tfull[r.slot], n0, grow);
+          r.advance(TSTAGES);
+          ++issued;
         }
-        uint8_t* st = smem + s * STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[s], TX_BYTES);
-        tma_load_2d(st, &tm_x, &full[s], kt * BK, m0);
-        tma_load_2d(st + A_BYTES + B_BYTES, &tm_p, &full[s], n0, kt * (BK / 8));
-        const int grow = (kt * BK) / p.G;
-        tma_load_2d(st + A_BYTES + B_BYTES + P_BYTES, &tm_s, &full[s], n0, grow);
-        tma_load_2d(st + A_BYTES + B_BYTES + P_BYTES + SZ_BYTES, &tm_z, &full[s], n0, grow);
-        ++issued;
       }
-      for (int kt = max(0, issued - STAGES); kt < issued; ++kt) {
-        mbar_wait(&full[kt % STAGES], (kt / STAGES) & 1);
+      // Never leave with copies in flight: wait for the newest phase of every slot used.
+      const long long n = issued < TSTAGES ? issued : TSTAGES;
+      for (long long i = 0; i < n; ++i) {
+        if (r.slot == 0) { r.slot = TSTAGES; r.phase ^= 1u; }
+        --r.slot;
+        mbar_wait(&tfull[r.slot], r.phase);
       }
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0) {
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        if (!mbar_wait(&full[s], ph)) break;
-        if (!mbar_wait(&bfull[s], ph)) break;
+      Ring t, b;
+      bool ok = true;
+      int local = 0;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++local) {
+        const int a = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&accempty[a], aph ^ 1u)) { ok = false; break; }
         tc_fence_after();
-        uint8_t* st = smem + s * STAGE_BYTES;
-        const uint64_t adesc = umma_desc_sw128(smem_u32(st));
-        const uint64_t bdesc = umma_desc_sw128(smem_u32(st + A_BYTES));
+        const uint32_t dtmem = tmem_base + a * ACC_COLS;
+        for (int kt = 0; kt < KT; ++kt) {
+          if (!mbar_wait(&tfull[t.slot], t.phase) || !mbar_wait(&bfull[b.slot], b.phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(tring + t.slot * T_BYTES));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(bring + b.slot * B_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          // advance 16 fp16 = 32 bytes along K inside the swizzled rows
-          tc_mma_f16(tmem_base, adesc + static_cast<uint64_t>(kk * 2),
-                     bdesc + static_cast<uint64_t>(kk * 2), IDESC, (kt | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // advance 16 fp16 = 32 bytes along K inside the swizzled rows
+            tc_mma_f16(dtmem, adesc + static_cast<uint64_t>(kk * 2),
+                       bdesc + static_cast<uint64_t>(kk * 2), IDESC, (kt | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&tempty[t.slot]);
+          tc_commit(&bempty[b.slot]);
+          t.advance(TSTAGES);
+          b.advance(BSTAGES);
         }
-        tc_commit(&empty[s]);
+        if (ok) tc_commit(&accfull[a]);
       }
-      tc_commit(accfull);   // also issued on the abort path: tracks whatever is in flight
+      tc_commit(drain);   // completes once every MMA this thread issued has finished
     }
-  } else {
+  } else if (warp < EPI_WARP0) {
     // ------------------------------ dequantisers --------------------------
     const int t = threadIdx.x - 64;   // column of the tile owned by this thread
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (!mbar_wait(&full[s], (kt / STAGES) & 1)) break;
-      uint8_t* st = smem + s * STAGE_BYTES;
-      const __half sv = reinterpret_cast<const __half*>(st + A_BYTES + B_BYTES + P_BYTES)[t];
-      const __half zv =
-          reinterpret_cast<const __half*>(st + A_BYTES + B_BYTES + P_BYTES + SZ_BYTES)[t];
-      const uint32_t ss = static_cast<uint32_t>(__half_as_ushort(sv)) * 0x10001u;
-      const uint32_t zc =
-          static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
-          (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
-      const uint32_t* pk = reinterpret_cast<const uint32_t*>(st + A_BYTES + B_BYTES);
-      uint8_t* brow = st + A_BYTES + t * 128;
+    Ring tr, br;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!warp_wait(&tfull[tr.slot], tr.phase) || !warp_wait(&bempty[br.slot], br.phase ^ 1u)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* st = tring + tr.slot * T_BYTES;
+        const __half sv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES)[t];
+        const __half zv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES + SZ_BYTES)[t];
+        const uint32_t ss = static_cast<uint32_t>(__half_as_ushort(sv)) * 0x10001u;
+        const uint32_t zc =
+            static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
+            (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
+        const uint32_t* pk = reinterpret_cast<const uint32_t*>(st + A_BYTES);
+        uint32_t w[BK / 8];
 #pragma unroll
-      for (int c = 0; c < BK / 8; ++c) {
-        const uint32_t w = pk[c * BN + t];
-        const uint4 v = dequant_word_nat(w, zc, ss);
-        *reinterpret_cast<uint4*>(brow + ((c ^ (t & 7)) << 4)) = v;
+        for (int c = 0; c < BK / 8; ++c) w[c] = pk[c * BN + t];
+        uint8_t* brow = bring + br.slot * B_BYTES + t * 128;
+#pragma unroll
+        for (int c = 0; c < BK / 8; ++c) {
+          *reinterpret_cast<uint4*>(brow + ((c ^ (t & 7)) << 4)) = dequant_word_nat(w[c], zc, ss);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[br.slot]);
+        tr.advance(TSTAGES);
+        br.advance(BSTAGES);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&bfull[s]);
     }
-
+  } else {
     // ------------------------------ epilogue -------------------------------
-    const bool acc_ok = mbar_wait(accfull, 0);
-    __syncwarp();   // tcgen05.ld is .sync.aligned: reconverge after the wait loop
-    tc_fence_after();
-    if (acc_ok) {
-      const int quarter = warp & 3;
-      const int chalf = (warp - 2) >> 2;
-      const int row = quarter * 32 + lane;
-      const int m = m0 + row;
+    const int quarter = warp & 3;   // TMEM lanes this warp may access
+    const int row = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
+      const int a = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!warp_wait(&accfull[a], aph)) break;
+      tc_fence_after();
+      const int m = (tile % p.m_tiles) * BM + row;
+      const int n0 = (tile / p.m_tiles) * BN;
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        const int col = chalf * 128 + cc * 32;
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        const int col = cc * 32;
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + col, r);
+        tmem_ld_32x32b_x32(tmem_base + a * ACC_COLS + (static_cast<uint32_t>(quarter * 32) << 16) + col, r);
         tmem_ld_wait();
         if (m < p.M) {
           __half* yrow = p.y + static_cast<long long>(m) * p.ldy + n0 + col;
@@ -232,14 +309,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&accempty[a]);
     }
   }
 
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    // The accumulator barrier completes once every issued MMA has finished.
-    mbar_wait(accfull, 0);
+    mbar_wait(drain, 0);   // every issued MMA has finished before TMEM is released
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

@@ -73,7 +73,7 @@ int current_device_state(DeviceState** out) {
     auto set_decode = [](auto kern) {
       return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
                  cudaSuccess &&
-             cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+             cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) ==
                  cudaSuccess;
     };
     if (!set_decode(decode::decode_gemv_tma_kernel<1>) ||
@@ -159,11 +159,50 @@ dim3 grid_2d(int64_t x, int64_t y) {
 // ---------------------------------------------------------------------------
 // GEMM launchers
 // ---------------------------------------------------------------------------
+// Decode launch plan: ring depth, grid (one resident wave) and workspace.
+struct DecodePlan {
+  int MT = 1, nst = 2, grid = 0, kstages = 0, chunks = 0;
+  long long units = 0;
+  size_t smem = 0;
+  size_t partial_bytes = 0, counter_bytes = 0;
+  size_t workspace() const { return partial_bytes + counter_bytes; }
+};
+
+int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
+  DecodePlan d;
+  d.MT = (M + 7) / 8;
+  d.kstages = (K + decode::KSTAGE - 1) / decode::KSTAGE;
+  d.chunks = (N + decode::BN - 1) / decode::BN;
+  d.units = static_cast<long long>(d.chunks) * d.kstages;
+  const int sbytes = decode::stage_bytes(M);
+  // Ring depth: ~100 KB of stages (>= 2, <= 8) so two CTAs can share an SM.
+  int nst = (100 * 1024 - decode::red_bytes(d.MT)) / sbytes;
+  nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
+  d.nst = nst;
+  d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) +
+           2 * nst * sizeof(uint64_t) + 16;
+  const int resident = decode_ctas_per_sm(dev, d.MT, d.smem);
+  if (resident <= 0) return W4A16_ERR_LAUNCH;
+  long long grid = static_cast<long long>(resident) * dev.num_sms;
+  if (grid > d.units) grid = d.units;
+  d.grid = static_cast<int>(grid);
+  d.partial_bytes = static_cast<size_t>(d.grid) * 2 * (d.MT * 8) * decode::BN * sizeof(float);
+  d.counter_bytes = decode::COUNTER_BYTES;
+  *out = d;
+  return W4A16_OK;
+}
+
 int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                       const __half* z, const __half* bias, __half* y, int M, int N, int K, int G,
-                      long long ldy, cudaStream_t stream) {
+                      long long ldy, void* workspace, int64_t workspace_bytes,
+                      cudaStream_t stream) {
+  DecodePlan d;
+  int st = plan_decode(dev, M, N, K, &d);
+  if (st != W4A16_OK) return st;
+  if (workspace == nullptr || workspace_bytes < static_cast<int64_t>(d.workspace()) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return W4A16_ERR_WORKSPACE;
   CUtensorMap tw, ts, tz, tx;
-  const int kstages = (K + decode::KSTAGE - 1) / decode::KSTAGE;
   if (!make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, qw, N, K / 8, N, decode::BN,
                    decode::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, N, K / G, N, decode::BN,
@@ -174,62 +213,31 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
                    CU_TENSOR_MAP_SWIZZLE_NONE)) {
     return W4A16_ERR_ALIGNMENT;
   }
-  const int chunks = (N + decode::BN - 1) / decode::BN;
-  const int MT = (M + 7) / 8;
-  const int sbytes = decode::stage_bytes(M);
-  // Ring depth: ~100 KB of stages (>= 2, <= 8) so two CTAs fit on an SM.
-  int nst = (100 * 1024 - decode::red_bytes(MT)) / sbytes;
-  nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
-  auto smem_for = [&](int stages) {
-    return 1024 + static_cast<size_t>(stages) * sbytes + decode::red_bytes(MT) +
-           2 * stages * sizeof(uint64_t);
-  };
-  const int resident = decode_ctas_per_sm(dev, MT, smem_for(nst));
-  if (resident <= 0) return W4A16_ERR_LAUNCH;
-  const int capacity = resident * dev.num_sms;
-  // Split K over a cluster while the grid still fits in one resident wave and
-  // each CTA keeps >= 2 stages. Cluster sizes divide the strip (1, 2, 4, 8).
-  int split = 1;
-  while (split < 8 && chunks * split * 2 <= capacity && kstages >= split * 4) split *= 2;
-  const int per_cta = (kstages + split - 1) / split;
-  if (nst > per_cta) nst = per_cta < 2 ? 2 : per_cta;
-  const size_t smem = smem_for(nst);
-
   decode::Params p;
   p.bias = bias;
   p.y = y;
+  p.counters = static_cast<unsigned*>(workspace);
+  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + d.counter_bytes);
   p.M = M;
   p.N = N;
   p.K = K;
   p.G = G;
+  p.g_shift = ((G & (G - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(G)) : -1;
   p.ldy = ldy;
-  p.stages_per_cta = per_cta;
-  p.num_stages = nst;
+  p.kstages = d.kstages;
+  p.units = d.units;
+  p.num_stages = d.nst;
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid_2d(chunks, split);
-  cfg.blockDim = dim3(decode::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = split;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  const dim3 grid(static_cast<unsigned>(d.grid), 1, 1);
   cudaError_t e;
-  switch (MT) {
-    case 1: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1>, tw, ts, tz, tx, p); break;
-    case 2: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2>, tw, ts, tz, tx, p); break;
-    case 3: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<3>, tw, ts, tz, tx, p); break;
-    default: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<4>, tw, ts, tz, tx, p); break;
+  switch (d.MT) {
+    case 1: decode::decode_gemv_tma_kernel<1><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
+    case 2: decode::decode_gemv_tma_kernel<2><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
+    case 3: decode::decode_gemv_tma_kernel<3><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
+    default: decode::decode_gemv_tma_kernel<4><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
   }
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return W4A16_ERR_LAUNCH;
-  }
-  return W4A16_OK;
+  e = cudaGetLastError();
+  return e == cudaSuccess ? W4A16_OK : W4A16_ERR_LAUNCH;
 }
 
 int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, const __half* z,
@@ -245,9 +253,9 @@ int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, 
   return W4A16_OK;
 }
 
-int launch_prefill(const __half* x, const int32_t* qw, const __half* s, const __half* z,
-                   const __half* bias, __half* y, int M, int N, int K, int G, long long ldy,
-                   cudaStream_t stream) {
+int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
+                   const __half* z, const __half* bias, __half* y, int M, int N, int K, int G,
+                   long long ldy, cudaStream_t stream) {
   CUtensorMap tx, tp, ts, tz;
   if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -266,9 +274,13 @@ int launch_prefill(const __half* x, const int32_t* qw, const __half* s, const __
   p.N = N;
   p.K = K;
   p.G = G;
+  p.g_shift = ((G & (G - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(G)) : -1;
   p.ldy = ldy;
+  p.m_tiles = (M + prefill::BM - 1) / prefill::BM;
+  p.n_tiles = (N + prefill::BN - 1) / prefill::BN;
   p.vec_store = (aligned16(y) && (ldy % 8) == 0) ? 1 : 0;
-  const dim3 grid = grid_2d((M + prefill::BM - 1) / prefill::BM, (N + prefill::BN - 1) / prefill::BN);
+  const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
   prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, tp, ts,
                                                                                        tz, p);
   W4A16_RETURN_IF_LAUNCH_FAILED();
@@ -292,13 +304,32 @@ const char* w4a16_strerror(int status) {
     case W4A16_ERR_LAUNCH: return "CUDA kernel launch failed";
     case W4A16_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) GPU";
     case W4A16_ERR_TIMEOUT: return "a kernel's bounded pipeline wait expired (device error flag set)";
+    case W4A16_ERR_WORKSPACE: return "workspace missing, too small or not 256-byte aligned";
     default: return "unknown w4a16 status";
   }
 }
 
+int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_size,
+                              int64_t* bytes_out) {
+  if (bytes_out == nullptr) return W4A16_ERR_INVALID;
+  *bytes_out = 0;
+  if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
+  if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
+  if (M == 0 || N == 0 || M > 32 || N % 8 != 0 || (N + decode::BN - 1) / decode::BN > decode::MAX_STRIPS)
+    return W4A16_OK;   // routes without workspace
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  DecodePlan d;
+  st = plan_decode(*dev, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), &d);
+  if (st != W4A16_OK) return st;
+  *bytes_out = static_cast<int64_t>(d.workspace());
+  return W4A16_OK;
+}
+
 int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                const void* bias, void* y, int64_t M, int64_t N, int64_t K, int64_t group_size,
-               int64_t ldy, void* stream) {
+               int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream) {
   if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
   if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
   if (ldy < N) return W4A16_ERR_INVALID;
@@ -321,10 +352,11 @@ int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const 
   if (!tma_ok) {
     return launch_decode_fallback(xh, qweight, sh, zh, bh, yh, M, n, k, g, ldy, s);
   }
-  if (M <= 32) {
-    return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy, s);
+  if (M <= 32 && (N + decode::BN - 1) / decode::BN <= decode::MAX_STRIPS) {
+    return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy,
+                             workspace, workspace_bytes, s);
   }
-  return launch_prefill(xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy, s);
+  return launch_prefill(*dev, xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy, s);
 }
 
 int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,

@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libw4a16_b2
 
 W4A16_OK = 0
 W4A16_ERR_TIMEOUT = -5
+W4A16_ERR_WORKSPACE = -6
 DTYPE_CODES = {torch.float16: 0, torch.float32: 1, torch.bfloat16: 2}
 
 # Every symbol the header declares, with its ctypes signature.
@@ -25,8 +26,10 @@ _vp = ctypes.c_void_p
 SIGNATURES = {
     "w4a16_version": ([], ctypes.c_int),
     "w4a16_strerror": ([ctypes.c_int], ctypes.c_char_p),
-    "w4a16_gemm": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp],
-                   ctypes.c_int),
+    "w4a16_gemm": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp,
+                    _c_i64, _vp], ctypes.c_int),
+    "w4a16_gemm_workspace_size": ([_c_i64, _c_i64, _c_i64, _c_i64, ctypes.POINTER(_c_i64)],
+                                  ctypes.c_int),
     "w4a16_quantize": ([_vp, ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_pack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_unpack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
@@ -98,3 +101,45 @@ def check_device_errors(device: torch.device | int | None = None) -> int:
         st = lib().w4a16_check_device_errors(stream_of(dev), ctypes.byref(flags))
     check(st, "w4a16_check_device_errors")
     return int(flags.value)
+
+
+# ---------------------------------------------------------------------------
+# GEMM workspace: one zeroed buffer per (device, stream), grown on demand. The
+# decode kernel leaves its counters zero after every launch, so the buffer is
+# reused without clearing. Superseded buffers are kept alive because a CUDA
+# graph captured earlier may still refer to them.
+# ---------------------------------------------------------------------------
+_ws_lock = threading.Lock()
+_ws_cache: dict[tuple[int, int], torch.Tensor] = {}
+_ws_retired: list[torch.Tensor] = []
+
+
+def gemm_workspace_bytes(M: int, N: int, K: int, G: int, device: torch.device) -> int:
+    out = ctypes.c_int64(0)
+    with torch.cuda.device(device):
+        st = lib().w4a16_gemm_workspace_size(M, N, K, G, ctypes.byref(out))
+    check(st, "w4a16_gemm_workspace_size")
+    return int(out.value)
+
+
+def gemm_workspace(nbytes: int, device: torch.device, stream: int) -> torch.Tensor | None:
+    """A zeroed, 256-byte-aligned scratch buffer of >= nbytes for this stream."""
+    if nbytes <= 0:
+        return None
+    key = (device.index, stream)
+    with _ws_lock:
+        ws = _ws_cache.get(key)
+        if ws is None or ws.numel() < nbytes:
+            if ws is not None:
+                _ws_retired.append(ws)
+            size = max(nbytes, 1 << 20)
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            _ws_cache[key] = ws
+        return ws
+
+
+def reset_workspaces() -> None:
+    """Zero every cached workspace (after a kernel reported W4A16_ERR_TIMEOUT)."""
+    with _ws_lock:
+        for ws in _ws_cache.values():
+            ws.zero_()

@@ -98,13 +98,21 @@ def w4a16_matmul(
         assert out.device == dev, "out must be on the inputs' CUDA device"
         y = out
 
-    lib = _lib.lib()
-    with torch.cuda.device(dev):
-        st = lib.w4a16_gemm(
-            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-            _lib.ptr(bias), y.data_ptr(), M, N, K, group_size, N, _lib.stream_of(dev))
-    _lib.check(st, "w4a16_gemm")
+    _launch(x, qweight, scales, zeros, bias, y, M, N, K, group_size, N)
     return y
+
+
+def _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy) -> None:
+    dev = x.device
+    with torch.cuda.device(dev):
+        stream = _lib.stream_of(dev)
+        ws = _lib.gemm_workspace(_lib.gemm_workspace_bytes(M, N, K, G, dev), dev, stream) \
+            if M > 0 and N > 0 else None
+        st = _lib.lib().w4a16_gemm(
+            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+            _lib.ptr(bias), y.data_ptr(), M, N, K, G, ldy,
+            _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
+    _lib.check(st, "w4a16_gemm")
 
 
 def w4a16_matmul_into(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
@@ -117,9 +125,4 @@ def w4a16_matmul_into(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor,
     """
     M, K = x.shape
     N = qweight.shape[1]
-    dev = x.device
-    with torch.cuda.device(dev):
-        st = _lib.lib().w4a16_gemm(
-            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-            _lib.ptr(bias), y.data_ptr(), M, N, K, group_size, ldy, _lib.stream_of(dev))
-    _lib.check(st, "w4a16_gemm")
+    _launch(x, qweight, scales, zeros, bias, y, M, N, K, group_size, ldy)
