@@ -2,29 +2,32 @@
 // on the 5th-generation tensor cores (tcgen05, accumulators in TMEM).
 //
 // Replaces the reference's Triton kernel (w4a16-kernel/src/w4a16/triton_kernel.py:62-128)
-// for large M. Persistent CTAs (one per SM) walk 128 x 256 output tiles; the
-// K loop of a tile runs in 64-wide steps. Warp roles:
+// for large M. Persistent CTAs (one per SM) walk 256 x 128 output tiles; the
+// K loop of a tile runs in 64-wide steps. Each dequantised weight tile feeds
+// two M=128 MMAs (the two 128-row halves of the x tile), which halves the
+// CUDA-core dequantisation work per tensor-core FLOP -- the dequantisation,
+// not the MMA, is what bounds a W4A16 GEMM. Warp roles:
 //
-//   warp 0       TMA producer: per step the x tile [128 x 64] fp16 (128-byte
-//                swizzle), the packed qweight tile [8 x 256] int32 and the
-//                step's scale and zero rows [256] fp16 into a 6-deep ring, all
+//   warp 0       TMA producer: per step the x tile [256 x 64] fp16 (128-byte
+//                swizzle), the packed qweight tile [8 x 128] int32 and the
+//                step's scale and zero rows [128] fp16 into a 4-deep ring, all
 //                on one transaction-counted mbarrier.
-//   warps 2..9   dequantisers: thread t owns column t of the tile; it unpacks
-//                the column's 8 words of the step (PRMT + LOP3 magic-number
+//   warps 2..9   dequantisers: two threads per tile column, each unpacking
+//                4 of the column's 8 words of the step (PRMT + LOP3 magic-number
 //                nibble extraction, exact (q - z), one fp16 multiply by s: the
 //                reference's rounding) and writes the fp16 weights K-major into
-//                a 128-byte-swizzled B tile of a 2-deep ring, then
+//                a 128-byte-swizzled B tile of a 3-deep ring, then
 //                fence.proxy.async so the tensor core may read them.
-//   warp 1       TMEM allocator (512 columns: two 256-column fp32
-//                accumulators) and single-thread MMA issuer:
-//                tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16, four per
-//                step; tcgen05.commit frees the ring slots and, after a tile's
-//                last step, hands its accumulator to the epilogue.
-//   warps 10..13 epilogue: each warp reads its 32-lane TMEM quarter with
-//                tcgen05.ld, rounds to fp16, adds the optional bias (rounded
-//                again, as W4A16Linear's separate add does) and stores; the
-//                double-buffered accumulator lets this overlap the next tile's
-//                main loop.
+//   warp 1       TMEM allocator (512 columns: two accumulator sets, each two
+//                128x128 fp32 halves) and single-thread MMA issuer:
+//                tcgen05.mma.cta_group::1.kind::f16, M=128 N=128 K=16, eight
+//                per step; tcgen05.commit frees the ring slots and, after a
+//                tile's last step, hands its accumulators to the epilogue.
+//   warps 10..13 epilogue: each warp reads its 32-lane TMEM quarter of both
+//                halves with tcgen05.ld, rounds to fp16, adds the optional bias
+//                (rounded again, as W4A16Linear's separate add does) and
+//                stores; the double-buffered accumulators let this overlap the
+//                next tile's main loop.
 //
 // Every mbarrier wait is bounded; on expiry the role raises the sticky device
 // error bit and leaves its loops, the producer drains its in-flight copies,
@@ -36,27 +39,30 @@
 namespace w4a16 {
 namespace prefill {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BM = 256;                      // two 128-row MMA halves
+constexpr int BMH = 128;
+constexpr int BN = 128;
 constexpr int BK = 64;
-constexpr int TSTAGES = 6;                   // TMA ring depth
-constexpr int BSTAGES = 2;                   // dequantised-B ring depth
-constexpr int A_BYTES = BM * BK * 2;         // 16384
-constexpr int P_BYTES = (BK / 8) * BN * 4;   // 8192
-constexpr int SZ_BYTES = BN * 2;             // 512
-constexpr int T_BYTES = A_BYTES + P_BYTES + 2 * SZ_BYTES;   // 25600 = 25 KiB per TMA stage
-constexpr int B_BYTES = BN * BK * 2;         // 32768
-constexpr int DQ_WARPS = 8;
+constexpr int TSTAGES = 4;                   // TMA ring depth
+constexpr int BSTAGES = 3;                   // dequantised-B ring depth
+constexpr int A_BYTES = BM * BK * 2;         // 32768
+constexpr int P_BYTES = (BK / 8) * BN * 4;   // 4096
+constexpr int SZ_BYTES = BN * 2;             // 256
+constexpr int T_BYTES = 37 * 1024;           // A + P + 2 SZ = 37376, padded to keep 1024-byte alignment
+constexpr int TX_BYTES = A_BYTES + P_BYTES + 2 * SZ_BYTES;
+constexpr int B_BYTES = BN * BK * 2;         // 16384
+constexpr int DQ_WARPS = 8;                  // two threads per tile column, 4 words each
 constexpr int EPI_WARPS = 4;
 constexpr int NUM_WARPS = 2 + DQ_WARPS + EPI_WARPS;
 constexpr int THREADS = NUM_WARPS * 32;
 constexpr int EPI_WARP0 = 2 + DQ_WARPS;
-constexpr uint32_t ACC_COLS = 256;
+constexpr uint32_t ACC_COLS = 2 * BN;        // one accumulator set: two 128-column halves
 constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = 1024 + TSTAGES * T_BYTES + BSTAGES * B_BYTES + BAR_BYTES;
-constexpr uint32_t IDESC = umma_idesc_f16_f32(BM, BN);
+constexpr uint32_t IDESC = umma_idesc_f16_f32(BMH, BN);
 
+static_assert(TX_BYTES <= T_BYTES, "TMA stage layout");
 static_assert(T_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
@@ -176,7 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint8_t* st = tring + r.slot * T_BYTES;
           const int kk = kt * BK;
           const int grow = p.g_shift >= 0 ? kk >> p.g_shift : kk / p.G;
-          mbar_arrive_expect_tx(&tfull[r.slot], T_BYTES);
+          mbar_arrive_expect_tx(&tfull[r.slot], TX_BYTES);
           tma_load_2d(st, &tm_x, &tfull[r.slot], kk, m0);
           tma_load_2d(st + A_BYTES, &tm_p, &tfull[r.slot], n0, kt * (BK / 8));
           tma_load_2d(st + A_BYTES + P_BYTES, &tm_s, &tfull[r.slot], n0, grow);
@@ -211,13 +217,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = umma_desc_sw128(smem_u32(tring + t.slot * T_BYTES));
+          const uint64_t adesc0 = umma_desc_sw128(smem_u32(tring + t.slot * T_BYTES));
+          const uint64_t adesc1 = umma_desc_sw128(smem_u32(tring + t.slot * T_BYTES + A_BYTES / 2));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(bring + b.slot * B_BYTES));
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             // advance 16 fp16 = 32 bytes along K inside the swizzled rows
-            tc_mma_f16(dtmem, adesc + static_cast<uint64_t>(kk * 2),
-                       bdesc + static_cast<uint64_t>(kk * 2), IDESC, (kt | kk) != 0 ? 1u : 0u);
+            const uint32_t acc = (kt | kk) != 0 ? 1u : 0u;
+            tc_mma_f16(dtmem, adesc0 + static_cast<uint64_t>(kk * 2),
+                       bdesc + static_cast<uint64_t>(kk * 2), IDESC, acc);
+            tc_mma_f16(dtmem + BN, adesc1 + static_cast<uint64_t>(kk * 2),
+                       bdesc + static_cast<uint64_t>(kk * 2), IDESC, acc);
           }
           tc_commit(&tempty[t.slot]);
           tc_commit(&bempty[b.slot]);
@@ -230,7 +240,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp < EPI_WARP0) {
     // ------------------------------ dequantisers --------------------------
-    const int t = threadIdx.x - 64;   // column of the tile owned by this thread
+    const int dt = threadIdx.x - 64;
+    const int t = dt & (BN - 1);      // column of the tile owned by this thread
+    const int c0 = (dt / BN) * 4;     // its 4 words (32 K) of the step's 8
     Ring tr, br;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -247,13 +259,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
             (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
         const uint32_t* pk = reinterpret_cast<const uint32_t*>(st + A_BYTES);
-        uint32_t w[BK / 8];
+        uint32_t w[4];
 #pragma unroll
-        for (int c = 0; c < BK / 8; ++c) w[c] = pk[c * BN + t];
+        for (int c = 0; c < 4; ++c) w[c] = pk[(c0 + c) * BN + t];
         uint8_t* brow = bring + br.slot * B_BYTES + t * 128;
 #pragma unroll
-        for (int c = 0; c < BK / 8; ++c) {
-          *reinterpret_cast<uint4*>(brow + ((c ^ (t & 7)) << 4)) = dequant_word_nat(w[c], zc, ss);
+        for (int c = 0; c < 4; ++c) {
+          *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) =
+              dequant_word_nat(w[c], zc, ss);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -265,20 +278,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ------------------------------ epilogue -------------------------------
     const int quarter = warp & 3;   // TMEM lanes this warp may access
-    const int row = quarter * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int a = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!warp_wait(&accfull[a], aph)) break;
       tc_fence_after();
-      const int m = (tile % p.m_tiles) * BM + row;
       const int n0 = (tile / p.m_tiles) * BN;
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        const int col = cc * 32;
+      for (int cc = 0; cc < 2 * BN / 32; ++cc) {
+        const int h = cc / (BN / 32);                 // which 128-row half
+        const int col = (cc % (BN / 32)) * 32;        // column within the tile
+        const int m = (tile % p.m_tiles) * BM + h * BMH + quarter * 32 + lane;
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + a * ACC_COLS + (static_cast<uint32_t>(quarter * 32) << 16) + col, r);
+        tmem_ld_32x32b_x32(tmem_base + a * ACC_COLS + h * BN + col +
+                               (static_cast<uint32_t>(quarter * 32) << 16), r);
         tmem_ld_wait();
         if (m < p.M) {
           __half* yrow = p.y + static_cast<long long>(m) * p.ldy + n0 + col;

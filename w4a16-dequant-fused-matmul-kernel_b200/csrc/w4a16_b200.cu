@@ -28,14 +28,10 @@ namespace {
 constexpr int kMaxDevices = 64;
 
 struct DeviceState {
-  static constexpr int kOcc = 64;
   bool checked = false;
   bool is_sm100 = false;
   bool attrs_set = false;
   int num_sms = 0;
-  int occ_n = 0;
-  long long occ_key[kOcc];
-  int occ_val[kOcc];
 };
 
 std::mutex g_mu;
@@ -72,9 +68,7 @@ int current_device_state(DeviceState** out) {
     }
     auto set_decode = [](auto kern) {
       return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
-                 cudaSuccess &&
-             cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) ==
-                 cudaSuccess;
+             cudaSuccess;
     };
     if (!set_decode(decode::decode_gemv_tma_kernel<1>) ||
         !set_decode(decode::decode_gemv_tma_kernel<2>) ||
@@ -122,34 +116,6 @@ bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Resident CTAs per SM of the decode kernel for a token-tile count and a
-// dynamic shared-memory size (cached per device; the set of keys is small).
-int decode_ctas_per_sm(DeviceState& dev, int MT, size_t smem) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  for (int i = 0; i < dev.occ_n; ++i) {
-    if (dev.occ_key[i] == static_cast<long long>(MT) * (1ll << 32) + static_cast<long long>(smem))
-      return dev.occ_val[i];
-  }
-  int r = 0;
-  cudaError_t e;
-  switch (MT) {
-    case 1: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<1>, decode::THREADS, smem); break;
-    case 2: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<2>, decode::THREADS, smem); break;
-    case 3: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<3>, decode::THREADS, smem); break;
-    default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, decode::decode_gemv_tma_kernel<4>, decode::THREADS, smem); break;
-  }
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  if (dev.occ_n < DeviceState::kOcc) {
-    dev.occ_key[dev.occ_n] = static_cast<long long>(MT) * (1ll << 32) + static_cast<long long>(smem);
-    dev.occ_val[dev.occ_n] = r;
-    ++dev.occ_n;
-  }
-  return r;
-}
-
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 dim3 grid_2d(int64_t x, int64_t y) {
@@ -165,7 +131,7 @@ struct DecodePlan {
   long long units = 0;
   size_t smem = 0;
   size_t partial_bytes = 0, counter_bytes = 0;
-  size_t workspace() const { return partial_bytes + counter_bytes; }
+  size_t workspace() const { return counter_bytes + partial_bytes; }
 };
 
 int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
@@ -175,15 +141,13 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   d.chunks = (N + decode::BN - 1) / decode::BN;
   d.units = static_cast<long long>(d.chunks) * d.kstages;
   const int sbytes = decode::stage_bytes(M);
-  // Ring depth: ~100 KB of stages (>= 2, <= 8) so two CTAs can share an SM.
-  int nst = (100 * 1024 - decode::red_bytes(d.MT)) / sbytes;
+  // Ring depth: ~190 KB of stages plus the reduction buffer (>= 2, <= 8), one CTA per SM.
+  int nst = (190 * 1024 - decode::red_bytes(d.MT)) / sbytes;
   nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
   d.nst = nst;
   d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) +
-           2 * nst * sizeof(uint64_t) + 16;
-  const int resident = decode_ctas_per_sm(dev, d.MT, d.smem);
-  if (resident <= 0) return W4A16_ERR_LAUNCH;
-  long long grid = static_cast<long long>(resident) * dev.num_sms;
+           3 * nst * sizeof(uint64_t) + 64;
+  long long grid = dev.num_sms;
   if (grid > d.units) grid = d.units;
   d.grid = static_cast<int>(grid);
   d.partial_bytes = static_cast<size_t>(d.grid) * 2 * (d.MT * 8) * decode::BN * sizeof(float);
@@ -209,7 +173,7 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
                    decode::SZ_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !make_map_2d(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, z, N, K / G, N, decode::BN,
                    decode::SZ_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, decode::KSTAGE, M,
+      !make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, decode::XBOX, M,
                    CU_TENSOR_MAP_SWIZZLE_NONE)) {
     return W4A16_ERR_ALIGNMENT;
   }
@@ -228,16 +192,28 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.units = d.units;
   p.num_stages = d.nst;
 
-  const dim3 grid(static_cast<unsigned>(d.grid), 1, 1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(d.grid), 1, 1);
+  cfg.blockDim = dim3(decode::threads_for(d.MT), 1, 1);
+  cfg.dynamicSmemBytes = d.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   cudaError_t e;
   switch (d.MT) {
-    case 1: decode::decode_gemv_tma_kernel<1><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
-    case 2: decode::decode_gemv_tma_kernel<2><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
-    case 3: decode::decode_gemv_tma_kernel<3><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
-    default: decode::decode_gemv_tma_kernel<4><<<grid, decode::THREADS, d.smem, stream>>>(tw, ts, tz, tx, p); break;
+    case 1: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1>, tw, ts, tz, tx, p); break;
+    case 2: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2>, tw, ts, tz, tx, p); break;
+    case 3: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<3>, tw, ts, tz, tx, p); break;
+    default: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<4>, tw, ts, tz, tx, p); break;
   }
-  e = cudaGetLastError();
-  return e == cudaSuccess ? W4A16_OK : W4A16_ERR_LAUNCH;
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_LAUNCH;
+  }
+  return W4A16_OK;
 }
 
 int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, const __half* z,
