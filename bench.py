@@ -402,6 +402,80 @@ def prefill_secondary(torch, w4a16, dev, args):
                          "kernel": "prefill::w4a16_tcgen05_kernel"}}
 
 
+def run_mlp(args):
+    """The decoder MLP-stack configuration: 80 blocks of gate/up [8192->28672]
+    (column-parallel, fused into one GEMM), SwiGLU and down [28672->8192]
+    (row-parallel, fp32 all-reduce over NCCL), at M=1 and M=2048 tokens.
+
+    Every block reads its own weights from HBM: 4 distinct weight sets are
+    cycled over the 80 blocks (>= 1.4 GB per GPU, far above L2). Each block
+    gets the same input, so the timed work is exactly the 80 blocks' GEMMs,
+    SwiGLUs and all-reduces without an activation-normalisation kernel."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from w4a16.parallel import W4A16MLP
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    D, H, G, L, NSETS = 8192, 28672, 128, 80, 4
+    blocks = []
+    for i in range(NSETS):
+        gen = torch.Generator(device=dev).manual_seed(1000 + i)
+        wg = (torch.randn(D, H, generator=gen, device=dev) * 0.02).half()
+        wu = (torch.randn(D, H, generator=gen, device=dev) * 0.02).half()
+        wd = (torch.randn(H, D, generator=gen, device=dev) * 0.02).half()
+        blocks.append(W4A16MLP.from_dense(wg, wu, wd, G))
+        del wg, wu, wd
+        torch.cuda.empty_cache()
+    per_block_bytes = sum(b.numel() * b.element_size() for b in blocks[0].buffers())
+    lines = []
+    for M in (1, 2048):
+        gen = torch.Generator(device=dev).manual_seed(7)
+        x = torch.randn(M, D, generator=gen, device=dev).half()
+
+        def step():
+            for l in range(L):
+                y = blocks[l % NSETS](x)
+            return y
+
+        for _ in range(max(1, args.warmup)):
+            step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = max(1, min(args.steps, 5))
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        flops = 2.0 * M * (2 * D * H + H * D) * L
+        lines.append({"config": {"workload": f"MLP stack 80 x (gate/up {D}->{H}, down {H}->{D}) G=128",
+                                 "M": M, "parallelism": f"tp{world}", "weights_per_gpu_per_block_bytes": per_block_bytes},
+                      "ms_per_step": ms, "hbm_gbs_per_gpu": per_block_bytes * L / (ms * 1e-3) / 1e9,
+                      "tflops_total": flops / (ms * 1e-3) / 1e12, "n_gpus": world, "steps": steps})
+    if rank == 0:
+        for ln in lines:
+            print(json.dumps(ln), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -411,10 +485,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the M=4096 secondary line")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--config", choices=["decode", "mlp"], default="decode",
+                    help="decode: the headline line; mlp: the 80-block MLP-stack configuration")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
+    if args.config == "mlp":
+        return run_mlp(args)
     return run_ours(args)
 
 

@@ -77,6 +77,28 @@ int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales,
                int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * w4a16_gemm with an fp32 output and no rounding (and no bias): the partial
+ * sums of a K-sharded (row-parallel) layer, summed across GPUs before the one
+ * final fp16 rounding, so a sharded layer matches the unsharded result.
+ * y: fp32, row m at y + m*ldy. Same requirements and workspace as w4a16_gemm.
+ * No reference counterpart: the reference has no multi-GPU path.
+ */
+int w4a16_gemm_f32(const void* x, const int32_t* qweight, const void* scales,
+                   const void* zeros, float* y, int64_t M, int64_t N, int64_t K,
+                   int64_t group_size, int64_t ldy, void* workspace,
+                   int64_t workspace_bytes, void* stream);
+
+/*
+ * SwiGLU of a fused gate/up projection: h[m, n] = silu(g) * u with
+ * g = gate_up[m, n] and u = gate_up[m, N + n] (fp16 in, fp32 math, one fp16
+ * rounding). gate_up rows have pitch ld_in >= 2N, h rows pitch ld_out >= N.
+ * No reference counterpart: it joins the projections of the MLP block the
+ * benchmark configuration names.
+ */
+int w4a16_swiglu(const void* gate_up, void* h, int64_t M, int64_t N, int64_t ld_in,
+                 int64_t ld_out, void* stream);
+
+/*
  * Bytes of workspace w4a16_gemm needs for this shape on the current device
  * (0 for shapes whose kernels need none). No reference counterpart: the
  * reference's kernels never split K across thread blocks.

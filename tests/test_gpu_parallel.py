@@ -1,0 +1,139 @@
+"""Tensor-parallel layers on the GPU: fp32-output GEMM, SwiGLU, the column /
+row-parallel layers and the MLP block against the numpy oracle; with two or
+more GPUs visible, also as NCCL ranks against the unsharded result."""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle
+from helpers import gpu_case, np_
+from tolerance import assert_gemm_close
+from w4a16 import quantize_weight, swiglu, w4a16_matmul_f32
+from w4a16.parallel import ColumnParallelW4A16Linear, RowParallelW4A16Linear, W4A16MLP
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+
+
+def _oracle_f32(X, qw, s, z, G):
+    W = oracle.dequantize_weight(np_(qw), np_(s), np_(z), G).astype(np.float32)
+    return np_(X).astype(np.float32) @ W
+
+
+def _silu_mul(g, u):
+    g = g.astype(np.float32)
+    return (g / (1.0 + np.exp(-g)) * u.astype(np.float32)).astype(np.float16)
+
+
+def _mlp_oracle(X, gate, up, down, G):
+    g = oracle.reference_w4a16(np_(X), *(np_(t) for t in gate), G)
+    u = oracle.reference_w4a16(np_(X), *(np_(t) for t in up), G)
+    h = _silu_mul(g, u)
+    return oracle.reference_w4a16(h, *(np_(t) for t in down), G)
+
+
+@pytest.mark.parametrize("M", [1, 5, 40, 300])
+def test_fp32_output_gemm(M):
+    X, W = gpu_case(M, 1024, 264, 128, sigma=0.05, seed=M)
+    qw, s, z = quantize_weight(W, 128)
+    y = w4a16_matmul_f32(X, qw, s, z, 128)
+    assert y.dtype == torch.float32 and y.shape == (M, 264)
+    ref = _oracle_f32(X, qw, s, z, 128)
+    err = np.abs(np_(y) - ref)
+    assert np.all(err <= 1e-4 + 1e-5 * np.abs(ref)), err.max()
+
+
+def test_swiglu_matches_fp32_reference():
+    gu = torch.randn(7, 2 * 136, device="cuda").half() * 3
+    h = swiglu(gu)
+    ref = _silu_mul(np_(gu[:, :136]), np_(gu[:, 136:]))
+    assert np.max(np.abs(np_(h).astype(np.float32) - ref.astype(np.float32))) <= 2e-3 * (1 + np.abs(ref).max())
+
+
+@pytest.mark.parametrize("M", [1, 64])
+def test_single_rank_layers_and_mlp(M):
+    D, H, G = 512, 1024, 128
+    X, Wg = gpu_case(M, D, H, G, sigma=0.05, seed=1)
+    _, Wu = gpu_case(1, D, H, G, sigma=0.05, seed=2)
+    _, Wd = gpu_case(1, H, D, G, sigma=0.05, seed=3)
+    col = ColumnParallelW4A16Linear.from_quantized(*quantize_weight(Wg, G), G)
+    qg = quantize_weight(Wg, G)
+    assert_gemm_close(np_(col(X, gather=True)), oracle.reference_w4a16(np_(X), *(np_(t) for t in qg), G), "col")
+    qd = quantize_weight(Wd, G)
+    row = RowParallelW4A16Linear.from_quantized(*qd, G)
+    Xh = torch.randn(M, H, device="cuda").half()
+    assert_gemm_close(np_(row(Xh)), oracle.reference_w4a16(np_(Xh), *(np_(t) for t in qd), G), "row")
+    mlp = W4A16MLP.from_dense(Wg, Wu, Wd, G)
+    y = mlp(X)
+    ref = _mlp_oracle(X, qg, quantize_weight(Wu, G), qd, G)
+    assert_gemm_close(np_(y), ref, "mlp")
+
+
+# ----------------------------------------------------------------------------- NCCL ranks
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank: int, world: int, port: int, q) -> None:
+    try:
+        for p in (os.path.join(ROOT, "w4a16-dequant-fused-matmul-kernel_b200"), ROOT,
+                  os.path.join(ROOT, "tests")):
+            sys.path.insert(0, p)
+        import datetime
+        import torch.distributed as dist
+        from helpers import gpu_case as case
+        from w4a16 import quantize_weight as quant, w4a16_matmul
+        from w4a16.parallel import ColumnParallelW4A16Linear as Col, W4A16MLP as MLP
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        D, H, G, M = 1024, 2048, 128, 4
+        X, Wg = case(M, D, H, G, sigma=0.05, seed=1, device=dev)
+        _, Wu = case(1, D, H, G, sigma=0.05, seed=2, device=dev)
+        _, Wd = case(1, H, D, G, sigma=0.05, seed=3, device=dev)
+        qg = quant(Wg, G)
+        full = w4a16_matmul(X, *qg, G)
+        y = Col.from_quantized(*qg, G)(X, gather=True)
+        col_err = float((y.float() - full.float()).abs().max())
+        mlp = MLP.from_dense(Wg, Wu, Wd, G)(X)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, col_err, mlp.cpu().numpy(), None))
+    except Exception as e:
+        q.put((rank, None, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_column_gather_and_mlp():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for rank, col_err, _, err in res:
+        assert err is None, f"rank {rank}: {err}"
+        assert col_err <= 1e-2, f"rank {rank}: gathered shards differ by {col_err}"
+    # the same block unsharded on one GPU
+    D, H, G, M = 1024, 2048, 128, 4
+    X, Wg = gpu_case(M, D, H, G, sigma=0.05, seed=1)
+    _, Wu = gpu_case(1, D, H, G, sigma=0.05, seed=2)
+    _, Wd = gpu_case(1, H, D, G, sigma=0.05, seed=3)
+    ref = _mlp_oracle(X, quantize_weight(Wg, G), quantize_weight(Wu, G), quantize_weight(Wd, G), G)
+    for rank, _, y, _ in res:
+        assert_gemm_close(y, ref, f"tp mlp rank {rank}")

@@ -67,7 +67,8 @@ __host__ __device__ constexpr int red_bytes(int MT) { return (ncw_for(MT) / 4) *
 
 struct Params {
   const __half* bias;
-  __half* y;
+  void* y;                // fp16, or fp32 when y_f32 (unrounded partial sums, no bias)
+  int y_f32;
   float* partials;        // [gridDim.x][2][MT*8][BN] fp32 partial sums of shared strips
   unsigned* counters;     // [strips] arrival counters, zero between launches
   int M, N, K, G;
@@ -124,9 +125,14 @@ __device__ __forceinline__ void consumer_sync() {
 }
 
 __device__ __forceinline__ void emit(const Params& p, int t, int n, float v) {
+  const long long o = static_cast<long long>(t) * p.ldy + n;
+  if (p.y_f32) {
+    static_cast<float*>(p.y)[o] = v;
+    return;
+  }
   __half h = __float2half_rn(v);
   if (p.bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(p.bias[n]));
-  p.y[static_cast<long long>(t) * p.ldy + n] = h;
+  static_cast<__half*>(p.y)[o] = h;
 }
 
 template <int MT>
@@ -472,7 +478,7 @@ __global__ void __launch_bounds__(FB_THREADS)
     decode_gemv_fallback_kernel(const __half* __restrict__ x, const int32_t* __restrict__ qw,
                                 const __half* __restrict__ scales,
                                 const __half* __restrict__ zeros, const __half* __restrict__ bias,
-                                __half* __restrict__ y, int M, int N, int K, int G,
+                                void* __restrict__ y, int y_f32, int M, int N, int K, int G,
                                 long long ldy) {
   __shared__ __half xs[32][FB_KCHUNK];
   const int n = blockIdx.x * FB_THREADS + threadIdx.x;
@@ -511,9 +517,14 @@ __global__ void __launch_bounds__(FB_THREADS)
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if (m < M) {
-        __half h = __float2half_rn(acc[m]);
-        if (bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(bias[n]));
-        y[static_cast<long long>(m) * ldy + n] = h;
+        const long long o = static_cast<long long>(m) * ldy + n;
+        if (y_f32) {
+          static_cast<float*>(y)[o] = acc[m];
+        } else {
+          __half h = __float2half_rn(acc[m]);
+          if (bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(bias[n]));
+          static_cast<__half*>(y)[o] = h;
+        }
       }
     }
   }

@@ -68,7 +68,8 @@ static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 struct Params {
   const __half* bias;
-  __half* y;
+  void* y;         // fp16, or fp32 when y_f32 (unrounded partial sums, no bias)
+  int y_f32;
   int M, N, K, G;
   int g_shift;     // log2(G) when G is a power of two, else -1
   long long ldy;
@@ -294,8 +295,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_32x32b_x32(tmem_base + a * ACC_COLS + h * BN + col +
                                (static_cast<uint32_t>(quarter * 32) << 16), r);
         tmem_ld_wait();
-        if (m < p.M) {
-          __half* yrow = p.y + static_cast<long long>(m) * p.ldy + n0 + col;
+        if (m < p.M && p.y_f32) {
+          float* yrow = static_cast<float*>(p.y) + static_cast<long long>(m) * p.ldy + n0 + col;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (n0 + col + v * 8 >= p.N) break;
+            if (p.vec_store) {
+              *reinterpret_cast<uint4*>(yrow + v * 8) = make_uint4(r[v * 8], r[v * 8 + 1], r[v * 8 + 2], r[v * 8 + 3]);
+              *reinterpret_cast<uint4*>(yrow + v * 8 + 4) =
+                  make_uint4(r[v * 8 + 4], r[v * 8 + 5], r[v * 8 + 6], r[v * 8 + 7]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) yrow[v * 8 + e] = __uint_as_float(r[v * 8 + e]);
+            }
+          }
+        } else if (m < p.M) {
+          __half* yrow = static_cast<__half*>(p.y) + static_cast<long long>(m) * p.ldy + n0 + col;
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int nb = n0 + col + v * 8;

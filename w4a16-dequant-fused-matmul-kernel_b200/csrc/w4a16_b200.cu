@@ -157,7 +157,7 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
 }
 
 int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
-                      const __half* z, const __half* bias, __half* y, int M, int N, int K, int G,
+                      const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                       long long ldy, void* workspace, int64_t workspace_bytes,
                       cudaStream_t stream) {
   DecodePlan d;
@@ -180,6 +180,7 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   decode::Params p;
   p.bias = bias;
   p.y = y;
+  p.y_f32 = y_f32;
   p.counters = static_cast<unsigned*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + d.counter_bytes);
   p.M = M;
@@ -217,20 +218,22 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
 }
 
 int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, const __half* z,
-                           const __half* bias, __half* y, int64_t M, int N, int K, int G,
+                           const __half* bias, void* y, int y_f32, int64_t M, int N, int K, int G,
                            long long ldy, cudaStream_t stream) {
   for (int64_t m0 = 0; m0 < M; m0 += 32) {
     const int mc = static_cast<int>(M - m0 < 32 ? M - m0 : 32);
     decode::decode_gemv_fallback_kernel<<<grid_2d((N + decode::FB_THREADS - 1) / decode::FB_THREADS, 1),
                                           decode::FB_THREADS, 0, stream>>>(
-        x + m0 * K, qw, s, z, bias, y + m0 * ldy, mc, N, K, G, ldy);
+        x + m0 * K, qw, s, z, bias,
+        static_cast<uint8_t*>(y) + m0 * ldy * (y_f32 ? sizeof(float) : sizeof(__half)), y_f32, mc,
+        N, K, G, ldy);
     W4A16_RETURN_IF_LAUNCH_FAILED();
   }
   return W4A16_OK;
 }
 
 int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
-                   const __half* z, const __half* bias, __half* y, int M, int N, int K, int G,
+                   const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                    long long ldy, cudaStream_t stream) {
   CUtensorMap tx, tp, ts, tz;
   if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
@@ -246,6 +249,7 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   prefill::Params p;
   p.bias = bias;
   p.y = y;
+  p.y_f32 = y_f32;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -254,13 +258,26 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.ldy = ldy;
   p.m_tiles = (M + prefill::BM - 1) / prefill::BM;
   p.n_tiles = (N + prefill::BN - 1) / prefill::BN;
-  p.vec_store = (aligned16(y) && (ldy % 8) == 0) ? 1 : 0;
+  p.vec_store = (aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0) ? 1 : 0;
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
   prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, tp, ts,
                                                                                        tz, p);
   W4A16_RETURN_IF_LAUNCH_FAILED();
   return W4A16_OK;
+}
+
+// h[m, n] = silu(g) * u with g = gate_up[m, n], u = gate_up[m, N + n]: the
+// SwiGLU between the fused gate/up projection and the down projection of an
+// MLP block, computed in fp32 and rounded once to fp16.
+__global__ void swiglu_kernel(const __half* __restrict__ gu, __half* __restrict__ h, int64_t M,
+                              int64_t N, int64_t ld_in, int64_t ld_out) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= M * N) return;
+  const int64_t m = idx / N, n = idx % N;
+  const float g = __half2float(gu[m * ld_in + n]);
+  const float u = __half2float(gu[m * ld_in + N + n]);
+  h[m * ld_out + n] = __float2half_rn(g / (1.0f + expf(-g)) * u);
 }
 
 }  // namespace
@@ -303,9 +320,12 @@ int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_siz
   return W4A16_OK;
 }
 
-int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
-               const void* bias, void* y, int64_t M, int64_t N, int64_t K, int64_t group_size,
-               int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+static int gemm_impl(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                     const void* bias, void* y, int y_f32, int64_t M, int64_t N, int64_t K,
+                     int64_t group_size, int64_t ldy, void* workspace, int64_t workspace_bytes,
+                     void* stream) {
   if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
   if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
   if (ldy < N) return W4A16_ERR_INVALID;
@@ -321,18 +341,50 @@ int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const 
   const __half* sh = static_cast<const __half*>(scales);
   const __half* zh = static_cast<const __half*>(zeros);
   const __half* bh = static_cast<const __half*>(bias);
-  __half* yh = static_cast<__half*>(y);
   const bool tma_ok = (N % 8 == 0) && aligned16(x) && aligned16(qweight) && aligned16(scales) &&
                       aligned16(zeros);
   const int n = static_cast<int>(N), k = static_cast<int>(K), g = static_cast<int>(group_size);
   if (!tma_ok) {
-    return launch_decode_fallback(xh, qweight, sh, zh, bh, yh, M, n, k, g, ldy, s);
+    return launch_decode_fallback(xh, qweight, sh, zh, bh, y, y_f32, M, n, k, g, ldy, s);
   }
   if (M <= 32 && (N + decode::BN - 1) / decode::BN <= decode::MAX_STRIPS) {
-    return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy,
-                             workspace, workspace_bytes, s);
+    return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g,
+                             ldy, workspace, workspace_bytes, s);
   }
-  return launch_prefill(*dev, xh, qweight, sh, zh, bh, yh, static_cast<int>(M), n, k, g, ldy, s);
+  return launch_prefill(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s);
+}
+
+extern "C" {
+
+int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+               const void* bias, void* y, int64_t M, int64_t N, int64_t K, int64_t group_size,
+               int64_t ldy, void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_impl(x, qweight, scales, zeros, bias, y, 0, M, N, K, group_size, ldy, workspace,
+                   workspace_bytes, stream);
+}
+
+int w4a16_gemm_f32(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                   float* y, int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t ldy,
+                   void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_impl(x, qweight, scales, zeros, nullptr, y, 1, M, N, K, group_size, ldy, workspace,
+                   workspace_bytes, stream);
+}
+
+int w4a16_swiglu(const void* gate_up, void* h, int64_t M, int64_t N, int64_t ld_in,
+                 int64_t ld_out, void* stream) {
+  if (M < 0 || N < 0 || ld_in < 2 * N || ld_out < N) return W4A16_ERR_INVALID;
+  if (M == 0 || N == 0) return W4A16_OK;
+  if (gate_up == nullptr || h == nullptr) return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  const int64_t total = M * N;
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks > 0x7fffffffLL) return W4A16_ERR_INVALID;
+  swiglu_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(gate_up), static_cast<__half*>(h), M, N, ld_in, ld_out);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
 }
 
 int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,

@@ -8,6 +8,9 @@ reference package (w4a16-kernel/src/w4a16/__init__.py:18-39):
     w4a16_matmul                                                    (gemm.py)
     W4A16Linear                                                     (linear.py)
 
+Tensor-parallel layers (column / row sharding over torch.distributed + NCCL)
+live in ``w4a16.parallel``.
+
 Everything computes in the hand-written sm_100a library ``libw4a16_b200.so``
 (C ABI in ``include/w4a16_b200.h``) -- there is one backend and no CPU or
 Triton fallback. Importing needs no GPU; calling needs a B200.
@@ -15,7 +18,7 @@ Triton fallback. Importing needs no GPU; calling needs a B200.
 from __future__ import annotations
 
 from ._lib import W4A16Error, check_device_errors
-from .gemm import w4a16_matmul
+from .gemm import swiglu, w4a16_matmul, w4a16_matmul_f32
 from .linear import W4A16Linear
 from .quant import dequantize_weight, pack_int4, quantize_weight, unpack_int4
 from .reference import dequant_then_matmul, fp16_matmul, reference_w4a16
@@ -30,6 +33,8 @@ __all__ = [
     "fp16_matmul",
     "w4a16_matmul",
     "W4A16Linear",
+    "w4a16_matmul_f32",
+    "swiglu",
     "W4A16Error",
     "check_device_errors",
 ]

@@ -108,11 +108,49 @@ def _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy) -> None:
         stream = _lib.stream_of(dev)
         ws = _lib.gemm_workspace(_lib.gemm_workspace_bytes(M, N, K, G, dev), dev, stream) \
             if M > 0 and N > 0 else None
-        st = _lib.lib().w4a16_gemm(
-            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-            _lib.ptr(bias), y.data_ptr(), M, N, K, G, ldy,
-            _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
+        if y.dtype == torch.float32:
+            assert bias is None
+            st = _lib.lib().w4a16_gemm_f32(
+                x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                y.data_ptr(), M, N, K, G, ldy, _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
+        else:
+            st = _lib.lib().w4a16_gemm(
+                x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                _lib.ptr(bias), y.data_ptr(), M, N, K, G, ldy,
+                _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
     _lib.check(st, "w4a16_gemm")
+
+
+def w4a16_matmul_f32(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
+                     out: Tensor | None = None) -> Tensor:
+    """``X @ dequant(qweight)`` as unrounded fp32 sums (no bias): the partial
+    result of a K-sharded layer, to be summed across ranks before rounding.
+    Same argument checks as :func:`w4a16_matmul`."""
+    w4a16_matmul(x[:0], qweight, scales, zeros, group_size)   # argument validation only
+    M, K = x.shape
+    N = qweight.shape[1]
+    if out is None:
+        out = torch.empty((M, N), device=x.device, dtype=torch.float32)
+    else:
+        assert out.shape == (M, N) and out.dtype == torch.float32 and out.is_contiguous()
+    _launch(x, qweight, scales, zeros, None, out, M, N, K, group_size, N)
+    return out
+
+
+def swiglu(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
+    """``silu(g) * u`` for ``gate_up = [g | u]`` of shape [M, 2H] (fp16) -> [M, H]."""
+    assert gate_up.is_cuda and gate_up.dtype == torch.float16 and gate_up.dim() == 2
+    assert gate_up.is_contiguous() and gate_up.shape[1] % 2 == 0
+    M, H2 = gate_up.shape
+    H = H2 // 2
+    if out is None:
+        out = torch.empty((M, H), device=gate_up.device, dtype=torch.float16)
+    dev = gate_up.device
+    with torch.cuda.device(dev):
+        st = _lib.lib().w4a16_swiglu(gate_up.data_ptr(), out.data_ptr(), M, H, H2, H,
+                                     _lib.stream_of(dev))
+    _lib.check(st, "w4a16_swiglu")
+    return out
 
 
 def w4a16_matmul_into(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
