@@ -56,10 +56,10 @@ constexpr int XBOX = 256;                     // K width of one x box (TMA box s
 constexpr int MAX_STRIPS = 16384;             // N <= 2,097,152 on the decode path
 constexpr size_t COUNTER_BYTES = MAX_STRIPS * sizeof(unsigned);
 
-// Consumer warps: 4 column quarters x KQ K parts. Up to 8 tokens (MT == 1)
-// 16 consumer warps (K quarters of 128); beyond that 8 (K halves of 256), so
-// that the larger accumulator sets still fit the register budget.
-__host__ __device__ constexpr int ncw_for(int MT) { return MT == 1 ? 16 : 8; }
+// Consumer warps: 4 column quarters x 2 K halves of 256 = 8 warps for every
+// token count. (16 warps with K quarters were measured 5% slower at M = 1 on
+// B200: the legacy MMA pipe, not warp count, bounds the consumers.)
+__host__ __device__ constexpr int ncw_for(int /*MT*/) { return 8; }
 __host__ __device__ constexpr int threads_for(int MT) { return 32 * (ncw_for(MT) + 2); }
 __host__ __device__ constexpr int x_bytes(int M) { return KSTAGE * 2 * M; }
 __host__ __device__ constexpr int stage_bytes(int M) { return W_BYTES + 2 * SZ_BYTES + x_bytes(M); }
