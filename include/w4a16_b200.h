@@ -146,6 +146,40 @@ int w4a16_dequantize(const int32_t* qweight, const void* scales, const void* zer
  */
 int w4a16_check_device_errors(void* stream, uint32_t* flags_out);
 
+/*
+ * w4a16_gemm without a workspace argument and without allocating anything.
+ * No counterpart in the reference (its kernels need no scratch at all).
+ *
+ * For callers that cannot allocate device memory at call time: a C or FFI
+ * host with no device allocator of its own, an engine whose memory planner
+ * has already handed out all device memory, or a plugin interface whose
+ * launch call passes no scratch buffer. The decode kernel's scratch (strip
+ * arrival counters and partial sums) lives instead in one static device
+ * array inside this library, W4A16_NOALLOC_SCRATCH_BYTES per device, whose
+ * address the library looks up once per device. Shapes whose decode launch
+ * would need more than that return W4A16_ERR_SCRATCH_LIMIT (on a 148-SM B200
+ * every shape fits: the need is 64 KiB + SMs * M-tiles * 64 KiB, at most
+ * about 4.7 MiB); prefill shapes need no scratch.
+ *
+ * The first call on each device does the set-up: it looks the array up,
+ * zeroes its counter region on `stream` and synchronises that stream. Make
+ * that first call before any stream capture; a first call made while
+ * `stream` is capturing returns W4A16_ERR_INVALID. The counters must be zero
+ * whenever a decode launch starts: set-up zeroes them and every completed
+ * launch leaves them zero, but a launch abandoned on W4A16_ERR_TIMEOUT may
+ * not. There is ONE scratch array per device, so calls whose kernels can run
+ * at the same time (different streams, threads or processes sharing a
+ * context, parallel graph branches) race on it and give wrong results: keep
+ * every call on one device ordered, or use w4a16_gemm with a workspace per
+ * stream. Arguments, routing and results are those of w4a16_gemm.
+ */
+#define W4A16_NOALLOC_SCRATCH_BYTES (5 * 1024 * 1024)
+#define W4A16_ERR_SCRATCH_LIMIT -7  /* shape needs more than the static scratch */
+int w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales,
+                       const void* zeros, const void* bias, void* y,
+                       int64_t M, int64_t N, int64_t K, int64_t group_size,
+                       int64_t ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -298,6 +298,9 @@ const char* w4a16_strerror(int status) {
     case W4A16_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) GPU";
     case W4A16_ERR_TIMEOUT: return "a kernel's bounded pipeline wait expired (device error flag set)";
     case W4A16_ERR_WORKSPACE: return "workspace missing, too small or not 256-byte aligned";
+    case W4A16_ERR_SCRATCH_LIMIT:
+      return "shape needs more scratch than w4a16_gemm_noalloc's static buffer holds "
+             "(use w4a16_gemm with a workspace)";
     default: return "unknown w4a16 status";
   }
 }
@@ -504,3 +507,84 @@ int w4a16_check_device_errors(void* stream, uint32_t* flags_out) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free GEMM (w4a16_gemm_noalloc)
+// ---------------------------------------------------------------------------
+// For callers that cannot allocate device memory when they launch (a C/FFI
+// host without a device allocator, an engine whose planner owns all device
+// memory, a plugin call that passes no scratch): the decode kernel's scratch
+// is this static array instead of a caller workspace. Layout as a workspace:
+// strip counters (decode::COUNTER_BYTES, must be zero when a launch starts)
+// at offset 0, partial sums after them. One array per device, so launches
+// that overlap in time race on it; callers keep them ordered.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[W4A16_NOALLOC_SCRATCH_BYTES];
+static_assert(decode::COUNTER_BYTES < W4A16_NOALLOC_SCRATCH_BYTES, "scratch holds the counters");
+
+namespace {
+struct NoallocScratch {
+  bool ready = false;
+  void* ptr = nullptr;
+};
+NoallocScratch g_noalloc[w4a16::kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: the array's device address
+// (host code never passes the symbol itself to a kernel) and its counter
+// region zeroed on `stream`, which is then synchronised. Refused while
+// `stream` is capturing, since neither step belongs in a graph.
+int noalloc_scratch(cudaStream_t stream, void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= w4a16::kMaxDevices) {
+    cudaGetLastError();
+    return W4A16_ERR_DEVICE;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoallocScratch& sc = g_noalloc[dev];
+  if (!sc.ready) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+      cudaGetLastError();
+      return W4A16_ERR_LAUNCH;
+    }
+    if (cap != cudaStreamCaptureStatusNone) return W4A16_ERR_INVALID;
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr ||
+        (reinterpret_cast<uintptr_t>(ptr) & 255u) != 0) {
+      cudaGetLastError();
+      return W4A16_ERR_LAUNCH;
+    }
+    if (cudaMemsetAsync(ptr, 0, decode::COUNTER_BYTES, stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess) {
+      cudaGetLastError();
+      return W4A16_ERR_LAUNCH;
+    }
+    sc.ptr = ptr;
+    sc.ready = true;
+  }
+  *out = sc.ptr;
+  return W4A16_OK;
+}
+}  // namespace
+
+extern "C" int w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales,
+                                  const void* zeros, const void* bias, void* y, int64_t M,
+                                  int64_t N, int64_t K, int64_t group_size, int64_t ldy,
+                                  void* stream) {
+  // The argument rules of w4a16_gemm, checked before any device work.
+  if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
+  if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
+  if (ldy < N) return W4A16_ERR_INVALID;
+  if (M == 0 || N == 0) return W4A16_OK;
+  if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || y == nullptr)
+    return W4A16_ERR_INVALID;
+  int64_t need = 0;
+  int st = w4a16_gemm_workspace_size(M, N, K, group_size, &need);
+  if (st != W4A16_OK) return st;
+  if (need > W4A16_NOALLOC_SCRATCH_BYTES) return W4A16_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  st = noalloc_scratch(static_cast<cudaStream_t>(stream), &scratch);
+  if (st != W4A16_OK) return st;
+  return gemm_impl(x, qweight, scales, zeros, bias, y, 0, M, N, K, group_size, ldy, scratch,
+                   W4A16_NOALLOC_SCRATCH_BYTES, stream);
+}

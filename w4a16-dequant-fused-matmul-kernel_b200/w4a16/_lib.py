@@ -38,6 +38,8 @@ SIGNATURES = {
     "w4a16_unpack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_dequantize": ([_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_check_device_errors": ([_vp, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+    "w4a16_gemm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                            _vp], ctypes.c_int),
 }
 
 _lock = threading.Lock()
