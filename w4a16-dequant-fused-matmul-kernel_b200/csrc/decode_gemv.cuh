@@ -17,9 +17,9 @@
 //    previous kernel; x, y and the workspace do). Back-to-back GEMMs thus
 //    overlap one launch's ramp-up with the previous launch's tail; measured
 //    on B200, a 22.5 MB TMA stream drops from 5.8 to 4.1 us per launch.
-//  * An x-permuter warp reorders each 8-element chunk of the stage's x slice
-//    to (k0,k4,k1,k5,k2,k6,k3,k7), so the consumers load MMA B fragments
-//    straight from shared memory.
+//  * Consumers read each 8-element chunk of x (k0..k7) from shared memory and
+//    reorder it to (k0,k4,k1,k5,k2,k6,k3,k7) with 4 PRMTs (ALU pipe, which has
+//    slack) to match the K order of their weight fragments.
 //  * Consumer warps dequantise in registers -- magic-number nibble extraction
 //    (OR the nibble into the mantissa of fp16 1024 or 64, then subtract
 //    1024+z or 64+z: exact), then one fp16 multiply by the scale, which
@@ -60,7 +60,7 @@ constexpr size_t COUNTER_BYTES = MAX_STRIPS * sizeof(unsigned);
 // token count. (16 warps with K quarters were measured 5% slower at M = 1 on
 // B200: the legacy MMA pipe, not warp count, bounds the consumers.)
 __host__ __device__ constexpr int ncw_for(int /*MT*/) { return 8; }
-__host__ __device__ constexpr int threads_for(int MT) { return 32 * (ncw_for(MT) + 2); }
+__host__ __device__ constexpr int threads_for(int MT) { return 32 * (ncw_for(MT) + 1); }
 __host__ __device__ constexpr int x_bytes(int M) { return KSTAGE * 2 * M; }
 __host__ __device__ constexpr int stage_bytes(int M) { return W_BYTES + 2 * SZ_BYTES + x_bytes(M); }
 __host__ __device__ constexpr int red_bytes(int MT) { return (ncw_for(MT) / 4) * (MT * 8) * BN * 4; }
@@ -118,7 +118,7 @@ __device__ __forceinline__ long long unit_begin(long long p, long long U, long l
   return (p * U) / P;
 }
 
-// Consumer-warp-only barrier (named barrier 1; producer and permuter do not take part).
+// Consumer-warp-only barrier (named barrier 1; the producer warp does not take part).
 template <int NCW>
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
   constexpr int KQ = NCW / 4;             // K parts per stage
   constexpr int KPART = KSTAGE / KQ;      // K per warp per stage (128 or 256)
   constexpr int NPAIR = KPART / 64;       // 64-K slices per warp per stage
+  static_assert(KPART == XBOX, "a warp's K part is one x box");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -154,8 +155,7 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
   const int sbytes = stage_bytes(M);
   float* red = reinterpret_cast<float*>(smem + nst * sbytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * sbytes + red_bytes(MT));
-  uint64_t* xready = full + nst;
-  uint64_t* empty = xready + nst;
+  uint64_t* empty = full + nst;
   int* flag = reinterpret_cast<int*>(empty + nst);
 
   const int warp = threadIdx.x >> 5;
@@ -174,7 +174,6 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
     pdl_launch_dependents();
     for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&xready[i], 1);
       mbar_init(&empty[i], NCW);
     }
     mbar_fence_init();
@@ -239,35 +238,9 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
   }
   pdl_wait();   // x, y and the workspace are only touched after the previous kernel
 
-  if (warp == 1) {
-    // ---------------------------- x permuter ------------------------------
-    // Each 8-element chunk (k0..k7) of the stage's x becomes (k0,k4,k1,k5,k2,k6,k3,k7).
-    int s = 0;
-    uint32_t ph = 0;
-    const int chunks = M * (KSTAGE / 8);
-    for (long long u = u0; u < u1; ++u) {
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(&full[s], ph);
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      __syncwarp();
-      if (!ok) break;
-      uint4* xs = reinterpret_cast<uint4*>(smem + s * sbytes + W_BYTES + 2 * SZ_BYTES);
-      for (int i = lane; i < chunks; i += 32) {
-        const uint4 v = xs[i];
-        xs[i] = make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632), prmt(v.y, v.w, 0x5410),
-                           prmt(v.y, v.w, 0x7632));
-      }
-      fence_proxy_async_smem();   // the ring slot is rewritten by TMA later
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&xready[s]);
-      if (++s == nst) { s = 0; ph ^= 1; }
-    }
-    return;
-  }
-
   // -------------------------------- consumers ---------------------------------
-  const int cw = warp - 2;
-  const int ctid = threadIdx.x - 64;
+  const int cw = warp - 1;
+  const int ctid = threadIdx.x - 32;
   const int cq = cw & 3;          // column quarter: 32 columns
   const int kq = cw >> 2;         // K part: packed rows [kq*KPART/8, (kq+1)*KPART/8) of the stage
   const int q = lane >> 2;        // MMA group id: columns 4q..4q+3 of the quarter
@@ -293,12 +266,16 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
     }
     if (ok) {
       bool got = true;
-      if (lane == 0) got = mbar_wait(&xready[s], ph);
+      if (lane == 0) got = mbar_wait(&full[s], ph);
       ok = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
       __syncwarp();   // orders the other lanes' shared-memory reads after lane 0's acquire
     }
     if (ok) {
       const uint8_t* st = smem + s * sbytes;
+      // Per-stage load bases: every load below is base + a compile-time offset. The
+      // warp's 32 packed rows all lie in x box kq (rows kq*32 .. kq*32+31 of the stage).
+      const uint8_t* wq = st + ((kq * (KPART / 8) + g) * BN + ccol) * 4;
+      const uint8_t* xq = st + W_BYTES + 2 * SZ_BYTES + kq * (XBOX * 2 * M) + q * (XBOX * 2) + g * 16;
       const int kbase = k * KSTAGE;
       const int g0 = p.g_shift >= 0 ? kbase >> p.g_shift : kbase / p.G;
       int gcur = -1;
@@ -330,18 +307,19 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
         }
 #pragma unroll
         for (int qq = 0; qq < 2; ++qq) {
-          const int iloc = kq * (KPART / 8) + pr * 8 + qq * 4 + g;   // packed row within the stage
-          const uint4 wv = *reinterpret_cast<const uint4*>(st + (iloc * BN + ccol) * 4);
+          // packed row kq*32 + roff + g of the stage
+          const int roff = pr * 8 + qq * 4;
+          const uint4 wv = *reinterpret_cast<const uint4*>(wq + roff * BN * 4);
           uint4 xv[MT];
 #pragma unroll
           for (int tt = 0; tt < MT; ++tt) {
-            const int tok = tt * 8 + q;
-            xv[tt] = make_uint4(0u, 0u, 0u, 0u);
-            if (tt == 0 ? has_x : tok < M) {
-              xv[tt] = *reinterpret_cast<const uint4*>(st + W_BYTES + 2 * SZ_BYTES +
-                                                       (iloc >> 5) * (XBOX * 2 * M) +
-                                                       tok * (XBOX * 2) + (iloc & 31) * 16);
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (tt == 0 ? has_x : tt * 8 + q < M) {
+              v = *reinterpret_cast<const uint4*>(xq + tt * 8 * (XBOX * 2) + roff * 16);
             }
+            // (k0..k7) -> pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7), the weight fragments' K order
+            xv[tt] = make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632),
+                                prmt(v.y, v.w, 0x5410), prmt(v.y, v.w, 0x7632));
           }
           uint32_t d[4][4];
           dequant_word_perm(wv.x, za[0], zb[0], ss[0], d[0]);

@@ -146,7 +146,7 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
   d.nst = nst;
   d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) +
-           3 * nst * sizeof(uint64_t) + 64;
+           2 * nst * sizeof(uint64_t) + 64;
   long long grid = dev.num_sms;
   if (grid > d.units) grid = d.units;
   d.grid = static_cast<int>(grid);
