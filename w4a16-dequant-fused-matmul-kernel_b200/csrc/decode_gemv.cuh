@@ -31,11 +31,14 @@
 //    product unchanged).
 //  * A strip covered by one CTA is reduced in shared memory and written
 //    directly. Each CTA shares at most two strips (its first and last) with
-//    neighbours: it parks those partial sums in a caller-provided workspace
-//    during the stream (plain stores), then after its last stage fences once
-//    and counts its arrival per strip; the last CTA to arrive sums all pieces
-//    in CTA order -- deterministic -- writes y and resets the counter, leaving
-//    the workspace clean for the next launch.
+//    neighbours. Its first strip ends early in its range: the consumers park
+//    that piece in the caller's workspace and an idle lane of the producer warp
+//    fences and counts the arrival, off the consumers' path. At the end, the
+//    CTA reads its last strip's counter: when every other piece has arrived
+//    (the usual case) it is the last arriver without publishing its own piece;
+//    otherwise it publishes and counts like the others. The last arriver sums
+//    all pieces in CTA order -- deterministic -- writes y and resets the
+//    counter, leaving the workspace clean for the next launch.
 #pragma once
 
 #include "common.cuh"
@@ -64,6 +67,10 @@ __host__ __device__ constexpr int threads_for(int MT) { return 32 * (ncw_for(MT)
 __host__ __device__ constexpr int x_bytes(int M) { return KSTAGE * 2 * M; }
 __host__ __device__ constexpr int stage_bytes(int M) { return W_BYTES + 2 * SZ_BYTES + x_bytes(M); }
 __host__ __device__ constexpr int red_bytes(int MT) { return (ncw_for(MT) / 4) * (MT * 8) * BN * 4; }
+// TMA destinations within a stage (W, S, Z, x box 0, x box 1) are 128-byte aligned.
+static_assert(W_BYTES % 128 == 0 && SZ_BYTES % 128 == 0 && (XBOX * 2) % 128 == 0 &&
+                  stage_bytes(1) % 1024 == 0,
+              "decode stage layout keeps TMA destinations 128-byte aligned");
 
 struct Params {
   const __half* bias;
@@ -156,7 +163,9 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
   float* red = reinterpret_cast<float*>(smem + nst * sbytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * sbytes + red_bytes(MT));
   uint64_t* empty = full + nst;
-  int* flag = reinterpret_cast<int*>(empty + nst);
+  uint64_t* piece_ready = empty + nst;   // consumers -> publisher: first-strip piece parked
+  uint64_t* published = piece_ready + 1; // publisher -> consumers: its arrival was counted
+  int* flag = reinterpret_cast<int*>(published + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -169,6 +178,13 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
   const int k_first = static_cast<int>(u0 - static_cast<long long>(c_first) * KS);
   const int c_last = static_cast<int>((u1 - 1) / KS);
   const int k_last = static_cast<int>((u1 - 1) - static_cast<long long>(c_last) * KS);
+  // A strip is "split" when other CTAs hold part of its K range. This CTA's first
+  // strip may be split (then it is its neighbours' last strip), and so may its
+  // last strip; when both are the same strip there is a single split segment.
+  const bool first_split = !(k_first == 0 && (c_last > c_first || k_last == KS - 1));
+  const bool last_split = c_last > c_first && k_last != KS - 1;
+  const bool first_early = first_split && c_last > c_first;        // published mid-stream
+  const bool final_split = last_split || (first_split && c_last == c_first);
 
   if (threadIdx.x == 0) {
     pdl_launch_dependents();
@@ -176,6 +192,8 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NCW);
     }
+    mbar_init(piece_ready, NCW);
+    mbar_init(published, 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -234,6 +252,22 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
         mbar_wait(&full[s], ph);
       }
     }
+    if (lane == 1 && first_early) {
+      // Publisher for the first (split) strip, off the consumers' path: once they
+      // have parked its piece, make it visible device-wide and count the arrival.
+      // (Release chain: consumers' stores -> mbarrier arrive -> this wait -> fence.)
+      pdl_wait();
+      int last = 0;
+      if (mbar_wait(piece_ready, 0)) {
+        __threadfence();
+        const long long lo = static_cast<long long>(c_first) * KS, hi = lo + KS - 1;
+        const long long pf = ((lo + 1) * P + U - 1) / U - 1;
+        const long long pl = ((hi + 1) * P + U - 1) / U - 1;
+        last = atomicAdd(&p.counters[c_first], 1u) == static_cast<unsigned>(pl - pf) ? 1 : 0;
+      }
+      flag[2] = last;
+      mbar_arrive(published);
+    }
     return;   // takes no part in the consumers' barriers below
   }
   pdl_wait();   // x, y and the workspace are only touched after the previous kernel
@@ -246,7 +280,15 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
   const int q = lane >> 2;        // MMA group id: columns 4q..4q+3 of the quarter
   const int g = lane & 3;         // MMA thread-in-group: packed row within a quad
   const int ccol = cq * 32 + 4 * q;
-  const bool has_x = q < M;       // lanes whose token of tile 0 exists
+  // x rows this lane feeds to its MMA column q of each token tile (token tt*8 + q)
+  uint32_t xmask[MT];
+  int xoff[MT];
+#pragma unroll
+  for (int tt = 0; tt < MT; ++tt) {
+    const bool valid = tt * 8 + q < M;
+    xmask[tt] = valid ? 0xFFFFFFFFu : 0u;
+    xoff[tt] = valid ? (tt * 8 + q) * (XBOX * 2) : 0;
+  }
 
   float acc[2][2][MT][4];         // [quad parity][column tile][token tile][fragment]
   int s = 0;
@@ -275,7 +317,7 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
       // Per-stage load bases: every load below is base + a compile-time offset. The
       // warp's 32 packed rows all lie in x box kq (rows kq*32 .. kq*32+31 of the stage).
       const uint8_t* wq = st + ((kq * (KPART / 8) + g) * BN + ccol) * 4;
-      const uint8_t* xq = st + W_BYTES + 2 * SZ_BYTES + kq * (XBOX * 2 * M) + q * (XBOX * 2) + g * 16;
+      const uint8_t* xq = st + W_BYTES + 2 * SZ_BYTES + kq * (XBOX * 2 * M) + g * 16;
       const int kbase = k * KSTAGE;
       const int g0 = p.g_shift >= 0 ? kbase >> p.g_shift : kbase / p.G;
       int gcur = -1;
@@ -313,9 +355,19 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
           uint4 xv[MT];
 #pragma unroll
           for (int tt = 0; tt < MT; ++tt) {
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (tt == 0 ? has_x : tt * 8 + q < M) {
-              v = *reinterpret_cast<const uint4*>(xq + tt * 8 * (XBOX * 2) + roff * 16);
+            uint4 v;
+            if constexpr (MT <= 2) {
+              // branch-free: lanes whose token does not exist read token 0's row and mask
+              // it (a divergent branch per quad costs more than the load)
+              v = *reinterpret_cast<const uint4*>(xq + xoff[tt] + roff * 16);
+              v.x &= xmask[tt];
+              v.y &= xmask[tt];
+              v.z &= xmask[tt];
+              v.w &= xmask[tt];
+            } else {
+              // (no register room for the masks at 3-4 token tiles: 9 warps share 4 register files)
+              v = make_uint4(0u, 0u, 0u, 0u);
+              if (xmask[tt]) v = *reinterpret_cast<const uint4*>(xq + xoff[tt] + roff * 16);
             }
             // (k0..k7) -> pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7), the weight fragments' K order
             xv[tt] = make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632),
@@ -362,85 +414,139 @@ __global__ void __launch_bounds__(threads_for(MT), 1)
       }
       consumer_sync<NCW>();
       const bool whole = (k == KS - 1) && static_cast<long long>(c) * KS >= u0;
-      const int nout = M * BN;
-      float* dst = p.partials + (static_cast<long long>(blockIdx.x) * 2 + (c == c_first ? 0 : 1)) *
-                                    (MT * 8) * BN;
-      for (int idx = ctid; idx < nout; idx += NCW * 32) {
-        const int t = idx / BN, cc = idx % BN;
-        float v = 0.0f;
+      if (whole) {
+        for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
+          const int t = idx / BN, cc = idx % BN;
+          float v = 0.0f;
 #pragma unroll
-        for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
-        if (whole) {
+          for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
           const int n = c * BN + cc;
           if (n < p.N) emit(p, t, n, v);
-        } else {
-          dst[t * BN + cc] = v;   // parked; published after the loop
         }
+      } else if (u != u1 - 1) {
+        // the first strip, split and not the final segment: park its piece (slot 0)
+        // and hand it to the publisher lane
+        float* dst = p.partials + static_cast<long long>(blockIdx.x) * 2 * (MT * 8) * BN;
+        for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
+          const int t = idx / BN, cc = idx % BN;
+          float v = 0.0f;
+#pragma unroll
+          for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
+          dst[t * BN + cc] = v;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(piece_ready);
       }
-      consumer_sync<NCW>();   // red[] is reused by the next segment
+      // (the final split segment keeps its piece in red[] for the fix-up below)
+      if (u != u1 - 1) consumer_sync<NCW>();   // red[] is reused by the next segment
     }
     if (++k == KS) { k = 0; ++c; }
   }
 
-  // ---------------- publish shared strips; the last CTA to arrive emits ----------------
-  const bool first_split = !(k_first == 0 && (c_last > c_first || k_last == KS - 1));
-  const bool last_split = c_last > c_first && k_last != KS - 1;
-  if (!first_split && !last_split) return;
-  __threadfence();
-  consumer_sync<NCW>();
-  // flag[j]: this CTA arrived last at strip j (0: first strip, 1: last strip);
-  // flag[2 + j]: the strip's first CTA; flag[4 + j]: whether that CTA holds the
-  // piece in its slot 1 (the strip is not its first one).
-  if (ctid < 2) {
-    const int j = ctid;
-    flag[j] = 0;
-    if (j == 0 ? first_split : last_split) {
-      const int cs = j == 0 ? c_first : c_last;
-      const long long lo = static_cast<long long>(cs) * KS, hi = lo + KS - 1;
-      const long long pf = ((lo + 1) * P + U - 1) / U - 1;
-      const long long pl = ((hi + 1) * P + U - 1) / U - 1;
-      const unsigned old = atomicAdd(&p.counters[cs], 1u);
-      const bool last = old == static_cast<unsigned>(pl - pf);
-      if (last) p.counters[cs] = 0u;   // last arrival: leave the workspace clean
-      flag[2 + j] = static_cast<int>(pf);
-      flag[4 + j] = static_cast<int>(pl);
-      flag[6 + j] = (unit_begin(pf, U, P) / KS == cs) ? 0 : 1;
-      flag[j] = last ? 1 : 0;
+  // ---------------- shared strips: the last CTA to arrive sums and emits ----------------
+  // Pieces are summed in CTA order whoever sums them, so y is deterministic. The
+  // strip's first CTA holds its piece in slot 1 (the strip is its last one) unless
+  // the strip is also its first; every later CTA holds it in slot 0.
+  auto piece_range = [&](int cs, int& pf, int& pl, int& pf_slot) {
+    const long long lo = static_cast<long long>(cs) * KS, hi = lo + KS - 1;
+    pf = static_cast<int>(((lo + 1) * P + U - 1) / U - 1);
+    pl = static_cast<int>(((hi + 1) * P + U - 1) / U - 1);
+    pf_slot = (unit_begin(pf, U, P) / KS == cs) ? 0 : 1;
+  };
+  // y[:, strip cs] = sum of the pieces pf..pl; this CTA's own piece comes from red[]
+  // when own_in_red (it was never written out), else from the workspace.
+  auto sum_strip = [&](int cs, bool own_in_red) {
+    int pf, pl, pf_slot;
+    piece_range(cs, pf, pl, pf_slot);
+    const int me = static_cast<int>(blockIdx.x);
+    for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
+      const int t = idx / BN, cc = idx % BN;
+      const long long off = static_cast<long long>(t) * BN + cc;
+      float own = 0.0f;
+      if (own_in_red) {
+#pragma unroll
+        for (int j = 0; j < KQ; ++j) own += red[(j * MT * 8 + t) * BN + cc];
+      }
+      constexpr int MAXP = 8;   // pieces fetched before summing (more are summed in a loop)
+      float v = 0.0f;
+      for (int base = pf; base <= pl; base += MAXP) {
+        float part[MAXP];
+#pragma unroll
+        for (int i = 0; i < MAXP; ++i) {
+          const int pp = base + i;
+          part[i] = 0.0f;
+          if (pp <= pl) {
+            if (pp == me && own_in_red) {
+              part[i] = own;
+            } else {
+              const int slot = (pp == pf) ? pf_slot : 0;
+              part[i] = __ldcg(p.partials + (static_cast<long long>(pp) * 2 + slot) * (MT * 8) * BN + off);
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < MAXP; ++i) v += part[i];
+      }
+      const int n = cs * BN + cc;
+      if (n < p.N) emit(p, t, n, v);
+    }
+  };
+
+  if (final_split) {
+    const int cs = c_last;
+    int pf, pl, pf_slot;
+    piece_range(cs, pf, pl, pf_slot);
+    // When this CTA starts a two-piece strip whose other CTA continues past it,
+    // that CTA published its piece early (its first strip), so usually it is
+    // already counted: then this CTA is last without writing its own piece or
+    // counting itself. (A strip with a middle CTA gets its pieces late; there
+    // the check would only add a round trip.)
+    const long long pl_end = unit_begin(pl + 1, U, P);   // one past the last unit of CTA pl
+    const bool early_partner = pf == static_cast<int>(blockIdx.x) && pl == pf + 1 &&
+                               (pl_end - 1) / KS > cs;
+    bool last = false;
+    if (early_partner) {
+      if (ctid == 0) {
+        unsigned cnt;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cnt) : "l"(p.counters + cs) : "memory");
+        flag[0] = cnt == 1u ? 1 : 0;
+      }
+      consumer_sync<NCW>();
+      last = flag[0] != 0;
+    }
+    if (!last) {
+      float* dst = p.partials + (static_cast<long long>(blockIdx.x) * 2 + (c_last == c_first ? 0 : 1)) *
+                                    (MT * 8) * BN;
+      for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
+        const int t = idx / BN, cc = idx % BN;
+        float v = 0.0f;
+#pragma unroll
+        for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
+        dst[t * BN + cc] = v;
+      }
+      consumer_sync<NCW>();
+      if (ctid == 0) {
+        __threadfence();
+        flag[1] = atomicAdd(&p.counters[cs], 1u) == static_cast<unsigned>(pl - pf) ? 1 : 0;
+      }
+      consumer_sync<NCW>();
+      last = flag[1] != 0;
+      if (last) __threadfence();   // acquire side: the others' pieces are read below
+    }
+    if (last) {
+      if (ctid == 0) p.counters[cs] = 0u;   // last arrival: leave the workspace clean
+      sum_strip(cs, true);
     }
   }
-  consumer_sync<NCW>();
-  __threadfence();
-  // Sum every CTA's piece of the strip in CTA order (deterministic). A CTA after
-  // the strip's first one always starts inside the strip, so its piece is in
-  // slot 0; the first CTA's piece is in slot 0 only if the strip is its first.
-  constexpr int MAXP = 8;   // pieces fetched before summing (more are summed in a loop)
-  const int nout = M * BN;
-  const int half = (flag[0] && flag[1]) ? (NCW * 32) / 2 : NCW * 32;
-  const int j = (flag[0] && flag[1]) ? (ctid >= half ? 1 : 0) : (flag[0] ? 0 : 1);
-  if (!flag[j]) return;
-  const int lt = (flag[0] && flag[1]) ? ctid - j * half : ctid;
-  const int cs = j == 0 ? c_first : c_last;
-  const int pf = flag[2 + j], pl = flag[4 + j], pf_slot = flag[6 + j];
-  for (int idx = lt; idx < nout; idx += half) {
-    const int t = idx / BN, cc = idx % BN;
-    const long long off = static_cast<long long>(t) * BN + cc;
-    float v = 0.0f;
-    for (int base = pf; base <= pl; base += MAXP) {
-      float part[MAXP];
-#pragma unroll
-      for (int i = 0; i < MAXP; ++i) {
-        const int pp = base + i;
-        part[i] = 0.0f;
-        if (pp <= pl) {
-          const int slot = (pp == pf) ? pf_slot : 0;
-          part[i] = __ldcg(p.partials + (static_cast<long long>(pp) * 2 + slot) * (MT * 8) * BN + off);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < MAXP; ++i) v += part[i];
+  if (first_early) {
+    // the publisher's verdict on the first strip
+    if (lane == 0) mbar_wait(published, 0);
+    __syncwarp();
+    if (flag[2]) {
+      __threadfence();
+      if (ctid == 0) p.counters[c_first] = 0u;
+      sum_strip(c_first, false);
     }
-    const int n = cs * BN + cc;
-    if (n < p.N) emit(p, t, n, v);
   }
 }
 

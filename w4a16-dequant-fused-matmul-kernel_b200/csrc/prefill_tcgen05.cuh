@@ -2,32 +2,39 @@
 // on the 5th-generation tensor cores (tcgen05, accumulators in TMEM).
 //
 // Replaces the reference's Triton kernel (w4a16-kernel/src/w4a16/triton_kernel.py:62-128)
-// for large M. Persistent CTAs (one per SM) walk 256 x 128 output tiles; the
-// K loop of a tile runs in 64-wide steps. Each dequantised weight tile feeds
-// two M=128 MMAs (the two 128-row halves of the x tile), which halves the
-// CUDA-core dequantisation work per tensor-core FLOP -- the dequantisation,
-// not the MMA, is what bounds a W4A16 GEMM. Warp roles:
+// for large M. Persistent CTAs (one per SM) walk 256 x bn output tiles (bn a
+// multiple of 32 in [128, 224], chosen per shape by the host); the K loop of a
+// tile runs in 64-wide steps.
+//
+// What bounds it on B200: every K step streams the tile's x rows [256 x 64]
+// and packed weights [8 x bn] from L2 into shared memory, and each SM sustains
+// only ~32 B/clk from L2. A 256 x 128 tile moves 36 KB per step for 512 cycles
+// of MMAs; a 256 x 224 tile moves 39 KB for 896 MMA cycles. Under load a TMA
+// load takes ~1.5 us to land, so the ring is 4 steps deep. The two M=128 x
+// N=bn accumulators fill most of TMEM, so the epilogue does not overlap the
+// next tile's MMAs; 8 epilogue warps keep that drain short. bn below 224 only
+// serves to round the tile count to whole waves of CTAs.
 //
 //   warp 0       TMA producer: per step the x tile [256 x 64] fp16 (128-byte
-//                swizzle), the packed qweight tile [8 x 128] int32 and the
-//                step's scale and zero rows [128] fp16 into a 4-deep ring, all
+//                swizzle), the packed qweight tile [8 x bn] int32 and the
+//                step's scale and zero rows [bn] fp16 into a 4-deep ring, all
 //                on one transaction-counted mbarrier.
-//   warps 2..9   dequantisers: two threads per tile column, each unpacking
-//                4 of the column's 8 words of the step (PRMT + LOP3 magic-number
-//                nibble extraction, exact (q - z), one fp16 multiply by s: the
+//   warps 2..17  dequantisers: two threads per tile column each unpack 4 of the
+//                column's 8 words of the step (PRMT + LOP3 magic-number nibble
+//                extraction, exact (q - z), one fp16 multiply by s: the
 //                reference's rounding) and writes the fp16 weights K-major into
-//                a 128-byte-swizzled B tile of a 3-deep ring, then
+//                a 128-byte-swizzled B tile of a 2-deep ring, then
 //                fence.proxy.async so the tensor core may read them.
-//   warp 1       TMEM allocator (512 columns: two accumulator sets, each two
-//                128x128 fp32 halves) and single-thread MMA issuer:
-//                tcgen05.mma.cta_group::1.kind::f16, M=128 N=128 K=16, eight
-//                per step; tcgen05.commit frees the ring slots and, after a
-//                tile's last step, hands its accumulators to the epilogue.
-//   warps 10..13 epilogue: each warp reads its 32-lane TMEM quarter of both
-//                halves with tcgen05.ld, rounds to fp16, adds the optional bias
-//                (rounded again, as W4A16Linear's separate add does) and
-//                stores; the double-buffered accumulators let this overlap the
-//                next tile's main loop.
+//   warp 1       TMEM allocator (512 columns: two bn-column accumulator halves)
+//                and single-thread MMA issuer: tcgen05.mma.cta_group::1.kind::f16,
+//                M=128 N=bn K=16, eight per step (both 128-row halves of x
+//                against one dequantised B tile); tcgen05.commit frees the ring
+//                slots and, after a tile's last step, hands the accumulators to
+//                the epilogue.
+//   warps 18..25 epilogue: two warps per 32-lane TMEM quarter (one per 128-row
+//                half) read the accumulators with tcgen05.ld, round to fp16,
+//                add the optional bias (rounded again, as W4A16Linear's separate
+//                add does) and store.
 //
 // Every mbarrier wait is bounded; on expiry the role raises the sticky device
 // error bit and leaves its loops, the producer drains its in-flight copies,
@@ -41,30 +48,35 @@ namespace prefill {
 
 constexpr int BM = 256;                      // two 128-row MMA halves
 constexpr int BMH = 128;
-constexpr int BN = 128;
+constexpr int BN_MAX = 224;                  // tile columns: runtime bn in [128, 224], bn % 32 == 0
+constexpr int BN_MIN = 128;
 constexpr int BK = 64;
-constexpr int TSTAGES = 4;                   // TMA ring depth
-constexpr int BSTAGES = 3;                   // dequantised-B ring depth
+constexpr int TSTAGES = 4;                   // TMA ring depth (covers ~1.5 us TMA latency under load)
+constexpr int BSTAGES = 2;                   // dequantised-B ring depth
 constexpr int A_BYTES = BM * BK * 2;         // 32768
-constexpr int P_BYTES = (BK / 8) * BN * 4;   // 4096
-constexpr int SZ_BYTES = BN * 2;             // 256
-constexpr int T_BYTES = 37 * 1024;           // A + P + 2 SZ = 37376, padded to keep 1024-byte alignment
-constexpr int TX_BYTES = A_BYTES + P_BYTES + 2 * SZ_BYTES;
-constexpr int B_BYTES = BN * BK * 2;         // 16384
-constexpr int DQ_WARPS = 8;                  // two threads per tile column, 4 words each
-constexpr int EPI_WARPS = 4;
+constexpr int P_BYTES = (BK / 8) * BN_MAX * 4;   // 7168 (room for bn = 224)
+constexpr int SZ_BYTES = 512;                // one row of bn <= 224 fp16, padded: TMA destinations are 128-byte aligned
+constexpr int T_BYTES = A_BYTES + P_BYTES + 2 * SZ_BYTES;   // 40960 = 40 KB
+constexpr int B_BYTES = BN_MAX * BK * 2;     // 28672
+constexpr int DQ_WARPS = 16;                 // two threads per tile column, 4 words each (256 columns of room)
+constexpr int EPI_WARPS = 8;                 // two per TMEM lane quarter
 constexpr int NUM_WARPS = 2 + DQ_WARPS + EPI_WARPS;
 constexpr int THREADS = NUM_WARPS * 32;
 constexpr int EPI_WARP0 = 2 + DQ_WARPS;
-constexpr uint32_t ACC_COLS = 2 * BN;        // one accumulator set: two 128-column halves
-constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+constexpr uint32_t TMEM_COLS = 512;          // two 128-row halves x bn columns (bn <= 224)
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = 1024 + TSTAGES * T_BYTES + BSTAGES * B_BYTES + BAR_BYTES;
-constexpr uint32_t IDESC = umma_idesc_f16_f32(BMH, BN);
 
-static_assert(TX_BYTES <= T_BYTES, "TMA stage layout");
 static_assert(T_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+static_assert(DQ_WARPS * 32 >= 2 * BN_MAX, "two dequantiser threads per tile column");
+static_assert(SZ_BYTES >= BN_MAX * 2, "scale/zero row slot");
+static_assert(A_BYTES % 128 == 0 && (A_BYTES + P_BYTES) % 128 == 0 &&
+                  (A_BYTES + P_BYTES + SZ_BYTES) % 128 == 0,
+              "every TMA destination in a stage must be 128-byte aligned");
+
+// TMA transaction bytes of one K step for a bn-column tile.
+__host__ __device__ constexpr int tx_bytes(int bn) { return A_BYTES + (BK / 8) * bn * 4 + 2 * bn * 2; }
 
 struct Params {
   const __half* bias;
@@ -74,6 +86,8 @@ struct Params {
   int g_shift;     // log2(G) when G is a power of two, else -1
   long long ldy;
   int m_tiles, n_tiles;
+  int bn;          // tile columns
+  uint32_t idesc;  // tcgen05 instruction descriptor for M=128, N=bn
   int vec_store;   // y and ldy allow 16-byte stores
 };
 
@@ -131,14 +145,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bfull = tempty + TSTAGES;
   uint64_t* bempty = bfull + BSTAGES;
   uint64_t* accfull = bempty + BSTAGES;
-  uint64_t* accempty = accfull + 2;
-  uint64_t* drain = accempty + 2;
+  uint64_t* accempty = accfull + 1;
+  uint64_t* drain = accempty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int KT = p.K / BK;
   const int ntiles = p.m_tiles * p.n_tiles;
+  const int bn = p.bn;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TSTAGES; ++s) {
@@ -149,10 +164,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bfull[j], DQ_WARPS);
       mbar_init(&bempty[j], 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&accfull[a], 1);
-      mbar_init(&accempty[a], EPI_WARPS);
-    }
+    mbar_init(accfull, 1);
+    mbar_init(accempty, EPI_WARPS);
     mbar_init(drain, 1);
     mbar_fence_init();
   }
@@ -172,18 +185,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       tma_prefetch_desc(&tm_p);
       tma_prefetch_desc(&tm_s);
       tma_prefetch_desc(&tm_z);
+      const uint32_t tx = static_cast<uint32_t>(tx_bytes(bn));
       Ring r;
       long long issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
         const int m0 = (tile % p.m_tiles) * BM;
-        const int n0 = (tile / p.m_tiles) * BN;
+        const int n0 = (tile / p.m_tiles) * bn;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u)) { ok = false; break; }
           uint8_t* st = tring + r.slot * T_BYTES;
           const int kk = kt * BK;
           const int grow = p.g_shift >= 0 ? kk >> p.g_shift : kk / p.G;
-          mbar_arrive_expect_tx(&tfull[r.slot], TX_BYTES);
+          mbar_arrive_expect_tx(&tfull[r.slot], tx);
           tma_load_2d(st, &tm_x, &tfull[r.slot], kk, m0);
           tma_load_2d(st + A_BYTES, &tm_p, &tfull[r.slot], n0, kt * (BK / 8));
           tma_load_2d(st + A_BYTES + P_BYTES, &tm_s, &tfull[r.slot], n0, grow);
@@ -207,11 +221,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       int local = 0;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++local) {
-        const int a = local & 1;
-        const uint32_t aph = (local >> 1) & 1;
-        if (!mbar_wait(&accempty[a], aph ^ 1u)) { ok = false; break; }
+        // the single accumulator set must have been drained by the epilogue
+        if (!mbar_wait(accempty, (local & 1) ^ 1u)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t dtmem = tmem_base + a * ACC_COLS;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&tfull[t.slot], t.phase) || !mbar_wait(&bfull[b.slot], b.phase)) {
             ok = false;
@@ -225,25 +237,26 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             // advance 16 fp16 = 32 bytes along K inside the swizzled rows
             const uint32_t acc = (kt | kk) != 0 ? 1u : 0u;
-            tc_mma_f16(dtmem, adesc0 + static_cast<uint64_t>(kk * 2),
-                       bdesc + static_cast<uint64_t>(kk * 2), IDESC, acc);
-            tc_mma_f16(dtmem + BN, adesc1 + static_cast<uint64_t>(kk * 2),
-                       bdesc + static_cast<uint64_t>(kk * 2), IDESC, acc);
+            tc_mma_f16(tmem_base, adesc0 + static_cast<uint64_t>(kk * 2),
+                       bdesc + static_cast<uint64_t>(kk * 2), p.idesc, acc);
+            tc_mma_f16(tmem_base + bn, adesc1 + static_cast<uint64_t>(kk * 2),
+                       bdesc + static_cast<uint64_t>(kk * 2), p.idesc, acc);
           }
           tc_commit(&tempty[t.slot]);
           tc_commit(&bempty[b.slot]);
           t.advance(TSTAGES);
           b.advance(BSTAGES);
         }
-        if (ok) tc_commit(&accfull[a]);
+        if (ok) tc_commit(accfull);
       }
       tc_commit(drain);   // completes once every MMA this thread issued has finished
     }
   } else if (warp < EPI_WARP0) {
     // ------------------------------ dequantisers --------------------------
     const int dt = threadIdx.x - 64;
-    const int t = dt & (BN - 1);      // column of the tile owned by this thread
-    const int c0 = (dt / BN) * 4;     // its 4 words (32 K) of the step's 8
+    const int t = dt & 255;              // column of the tile owned by this thread
+    const int c0 = (dt >> 8) * 4;        // its 4 words (32 K) of the step's 8
+    const bool active = t < bn;
     Ring tr, br;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -252,22 +265,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        const uint8_t* st = tring + tr.slot * T_BYTES;
-        const __half sv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES)[t];
-        const __half zv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES + SZ_BYTES)[t];
-        const uint32_t ss = static_cast<uint32_t>(__half_as_ushort(sv)) * 0x10001u;
-        const uint32_t zc =
-            static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
-            (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
-        const uint32_t* pk = reinterpret_cast<const uint32_t*>(st + A_BYTES);
-        uint32_t w[4];
+        if (active) {
+          const uint8_t* st = tring + tr.slot * T_BYTES;
+          const __half sv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES)[t];
+          const __half zv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES + SZ_BYTES)[t];
+          const uint32_t ss = static_cast<uint32_t>(__half_as_ushort(sv)) * 0x10001u;
+          const uint32_t zc =
+              static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
+              (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
+          // the packed tile is [8 rows x bn] int32, row-major
+          const uint32_t* pk = reinterpret_cast<const uint32_t*>(st + A_BYTES);
+          uint32_t w[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) w[c] = pk[(c0 + c) * BN + t];
-        uint8_t* brow = bring + br.slot * B_BYTES + t * 128;
+          for (int c = 0; c < 4; ++c) w[c] = pk[(c0 + c) * bn + t];
+          uint8_t* brow = bring + br.slot * B_BYTES + t * 128;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) =
-              dequant_word_nat(w[c], zc, ss);
+          for (int c = 0; c < 4; ++c) {
+            *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) = dequant_word_nat(w[c], zc, ss);
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -278,22 +293,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------ epilogue -------------------------------
-    const int quarter = warp & 3;   // TMEM lanes this warp may access
+    const int quarter = warp & 3;                 // TMEM lanes this warp may access
+    const int h = (warp - EPI_WARP0) >> 2;        // 128-row half of the tile
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
-      const int a = local & 1;
-      const uint32_t aph = (local >> 1) & 1;
-      if (!warp_wait(&accfull[a], aph)) break;
+      if (!warp_wait(accfull, local & 1)) break;
       tc_fence_after();
-      const int n0 = (tile / p.m_tiles) * BN;
+      const int n0 = (tile / p.m_tiles) * bn;
+      const int m = (tile % p.m_tiles) * BM + h * BMH + quarter * 32 + lane;
 #pragma unroll 1
-      for (int cc = 0; cc < 2 * BN / 32; ++cc) {
-        const int h = cc / (BN / 32);                 // which 128-row half
-        const int col = (cc % (BN / 32)) * 32;        // column within the tile
-        const int m = (tile % p.m_tiles) * BM + h * BMH + quarter * 32 + lane;
+      for (int col = 0; col < bn; col += 32) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + a * ACC_COLS + h * BN + col +
-                               (static_cast<uint32_t>(quarter * 32) << 16), r);
+        tmem_ld_32x32b_x32(tmem_base + h * bn + col + (static_cast<uint32_t>(quarter * 32) << 16), r);
         tmem_ld_wait();
         if (m < p.M && p.y_f32) {
           float* yrow = static_cast<float*>(p.y) + static_cast<long long>(m) * p.ldy + n0 + col;
@@ -340,7 +351,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&accempty[a]);
+      if (lane == 0) mbar_arrive(accempty);
     }
   }
 

@@ -15,6 +15,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -146,7 +147,7 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
   d.nst = nst;
   d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) +
-           2 * nst * sizeof(uint64_t) + 64;
+           (2 * nst + 2) * sizeof(uint64_t) + 64;
   long long grid = dev.num_sms;
   if (grid > d.units) grid = d.units;
   d.grid = static_cast<int>(grid);
@@ -232,17 +233,40 @@ int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, 
   return W4A16_OK;
 }
 
+// Tile width of the prefill kernel for this shape: the candidate with the least
+// modelled time = waves of tiles x cycles per K step, where a step costs the
+// larger of its MMAs (4 * bn cycles) and its L2 traffic (x tile 32 KB + 36 B per
+// column at ~31.5 B/clk per SM, measured on B200). Wider tiles reuse the x
+// tile more; narrower ones can round the tile count to whole waves.
+int choose_prefill_bn(int M, int N, int num_sms) {
+  const long long m_tiles = (M + prefill::BM - 1) / prefill::BM;
+  int best = prefill::BN_MAX;
+  double best_t = 1e300;
+  for (int bn = prefill::BN_MAX; bn >= prefill::BN_MIN; bn -= 32) {
+    const long long tiles = m_tiles * ((N + bn - 1) / bn);
+    const long long waves = (tiles + num_sms - 1) / num_sms;
+    const double step = std::max(4.0 * bn, (prefill::A_BYTES + 36.0 * bn) / 31.5);
+    const double t = static_cast<double>(waves) * step;
+    if (t < best_t * 0.999) {
+      best_t = t;
+      best = bn;
+    }
+  }
+  return best;
+}
+
 int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                    const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                    long long ldy, cudaStream_t stream) {
+  const int bn = choose_prefill_bn(M, N, dev.num_sms);
   CUtensorMap tx, tp, ts, tz;
   if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tp, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, qw, N, K / 8, N, prefill::BN,
+      !make_map_2d(&tp, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, qw, N, K / 8, N, bn,
                    prefill::BK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, N, K / G, N, prefill::BN, 1,
+      !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, N, K / G, N, bn, 1,
                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, z, N, K / G, N, prefill::BN, 1,
+      !make_map_2d(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, z, N, K / G, N, bn, 1,
                    CU_TENSOR_MAP_SWIZZLE_NONE)) {
     return W4A16_ERR_ALIGNMENT;
   }
@@ -257,7 +281,9 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.g_shift = ((G & (G - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(G)) : -1;
   p.ldy = ldy;
   p.m_tiles = (M + prefill::BM - 1) / prefill::BM;
-  p.n_tiles = (N + prefill::BN - 1) / prefill::BN;
+  p.n_tiles = (N + bn - 1) / bn;
+  p.bn = bn;
+  p.idesc = umma_idesc_f16_f32(prefill::BMH, static_cast<uint32_t>(bn));
   p.vec_store = (aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0) ? 1 : 0;
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
