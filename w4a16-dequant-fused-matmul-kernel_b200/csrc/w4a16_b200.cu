@@ -100,21 +100,63 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return g_encode;
 }
 
+// Encoded tensor maps, cached per host thread. A map is a pure function of the
+// encode arguments below (address, type, extents, pitch, box, swizzle), so a hit
+// is exactly the map an encode would produce; decode GEMMs re-use the same
+// weights every step, and the encode costs ~1 us of host time per map.
+struct MapKey {
+  const void* base;
+  uint64_t cols, rows, ld;
+  uint32_t box_cols, box_rows;
+  int dt, swz;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && cols == o.cols && rows == o.rows && ld == o.ld &&
+           box_cols == o.box_cols && box_rows == o.box_rows && dt == o.dt && swz == o.swz;
+  }
+};
+struct MapEntry {
+  bool valid = false;
+  MapKey key;
+  CUtensorMap map;
+};
+constexpr int kMapCacheSlots = 64;   // direct-mapped
+thread_local MapEntry t_map_cache[kMapCacheSlots];
+
+inline size_t map_slot(const MapKey& k) {
+  uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
+  h ^= (k.cols * 0x100000001B3ull) ^ (k.rows << 17) ^ (k.ld << 7) ^
+       (static_cast<uint64_t>(k.box_cols) << 40) ^ (static_cast<uint64_t>(k.box_rows) << 52) ^
+       (static_cast<uint64_t>(k.dt) << 3) ^ static_cast<uint64_t>(k.swz);
+  h ^= h >> 29;
+  return static_cast<size_t>(h % kMapCacheSlots);
+}
+
 // 2D row-major tensor map: `cols` contiguous elements per row, `rows` rows,
 // row pitch `ld` elements; box [box_cols x box_rows]; out-of-range boxes
 // read as zero.
 bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t cols,
                  uint64_t rows, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
                  CUtensorMapSwizzle swz) {
+  const MapKey key{base, cols, rows, ld, box_cols, box_rows, static_cast<int>(dt), static_cast<int>(swz)};
+  MapEntry& slot = t_map_cache[map_slot(key)];
+  if (slot.valid && slot.key == key) {
+    *m = slot.map;
+    return true;
+  }
   PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode_fn();
   if (enc == nullptr) return false;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {ld * static_cast<uint64_t>(esize)};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  if (enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  slot.valid = true;
+  slot.key = key;
+  slot.map = *m;
+  return true;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -84,8 +84,13 @@ def check(status: int, what: str) -> None:
         raise W4A16Error(status, what)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device: torch.device) -> int:
     """Raw cudaStream_t of torch's current stream on ``device``."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -119,12 +124,21 @@ _ws_cache: dict[tuple[int, int], torch.Tensor] = {}
 _ws_retired: list[torch.Tensor] = []
 
 
+_ws_size_cache: dict[tuple[int, int, int, int, int], int] = {}
+
+
 def gemm_workspace_bytes(M: int, N: int, K: int, G: int, device: torch.device) -> int:
-    out = ctypes.c_int64(0)
-    with torch.cuda.device(device):
-        st = lib().w4a16_gemm_workspace_size(M, N, K, G, ctypes.byref(out))
-    check(st, "w4a16_gemm_workspace_size")
-    return int(out.value)
+    """Workspace bytes for this shape on ``device`` (memoised: it depends only on
+    the shape and the device's SM count)."""
+    key = (M, N, K, G, device.index)
+    n = _ws_size_cache.get(key)
+    if n is None:
+        out = ctypes.c_int64(0)
+        with torch.cuda.device(device):
+            st = lib().w4a16_gemm_workspace_size(M, N, K, G, ctypes.byref(out))
+        check(st, "w4a16_gemm_workspace_size")
+        n = _ws_size_cache[key] = int(out.value)
+    return n
 
 
 def gemm_workspace(nbytes: int, device: torch.device, stream: int) -> torch.Tensor | None:

@@ -104,20 +104,22 @@ def w4a16_matmul(
 
 def _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy) -> None:
     dev = x.device
-    with torch.cuda.device(dev):
-        stream = _lib.stream_of(dev)
-        ws = _lib.gemm_workspace(_lib.gemm_workspace_bytes(M, N, K, G, dev), dev, stream) \
-            if M > 0 and N > 0 else None
-        if y.dtype == torch.float32:
-            assert bias is None
-            st = _lib.lib().w4a16_gemm_f32(
-                x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-                y.data_ptr(), M, N, K, G, ldy, _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
-        else:
-            st = _lib.lib().w4a16_gemm(
-                x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-                _lib.ptr(bias), y.data_ptr(), M, N, K, G, ldy,
-                _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
+    if dev.index != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            return _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy)
+    stream = _lib.stream_of(dev)
+    ws = _lib.gemm_workspace(_lib.gemm_workspace_bytes(M, N, K, G, dev), dev, stream) \
+        if M > 0 and N > 0 else None
+    if y.dtype == torch.float32:
+        assert bias is None
+        st = _lib.lib().w4a16_gemm_f32(
+            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+            y.data_ptr(), M, N, K, G, ldy, _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
+    else:
+        st = _lib.lib().w4a16_gemm(
+            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+            _lib.ptr(bias), y.data_ptr(), M, N, K, G, ldy,
+            _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
     _lib.check(st, "w4a16_gemm")
 
 
