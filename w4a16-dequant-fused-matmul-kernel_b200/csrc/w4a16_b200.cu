@@ -69,7 +69,9 @@ int current_device_state(DeviceState** out) {
     }
     auto set_decode = [](auto kern) {
       return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
-             cudaSuccess;
+                 cudaSuccess &&
+             cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) ==
+                 cudaSuccess;
     };
     if (!set_decode(decode::decode_gemv_tma_kernel<1>) ||
         !set_decode(decode::decode_gemv_tma_kernel<2>) ||
@@ -184,13 +186,15 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   d.chunks = (N + decode::BN - 1) / decode::BN;
   d.units = static_cast<long long>(d.chunks) * d.kstages;
   const int sbytes = decode::stage_bytes(M);
-  // Ring depth: ~190 KB of stages plus the reduction buffer (>= 2, <= 8), one CTA per SM.
-  int nst = (190 * 1024 - decode::red_bytes(d.MT)) / sbytes;
+  // Ring depth: ~190 KB of stages plus the reduction buffer per SM, split between the CTAs
+  // that share an SM (>= 2, <= 8 stages per CTA).
+  const int ring_budget = (decode::ctas_per_sm(d.MT) == 2 ? 108 : 190) * 1024;
+  int nst = (ring_budget - decode::red_bytes(d.MT)) / sbytes;
   nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
   d.nst = nst;
   d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) +
            (2 * nst + 2) * sizeof(uint64_t) + 64;
-  long long grid = dev.num_sms;
+  long long grid = static_cast<long long>(dev.num_sms) * decode::ctas_per_sm(d.MT);
   if (grid > d.units) grid = d.units;
   d.grid = static_cast<int>(grid);
   d.partial_bytes = static_cast<size_t>(d.grid) * 2 * (d.MT * 8) * decode::BN * sizeof(float);
