@@ -6,21 +6,22 @@
 // multiple of 32 in [128, 224], chosen per shape by the host); the K loop of a
 // tile runs in 64-wide steps.
 //
-// What bounds it on B200: every K step streams the tile's x rows [256 x 64]
-// and packed weights [8 x bn] from L2 into shared memory, and each SM sustains
-// only ~32 B/clk from L2. A 256 x 128 tile moves 36 KB per step for 512 cycles
-// of MMAs; a 256 x 224 tile moves 39 KB for 896 MMA cycles. Under load a TMA
-// load takes ~1.5 us to land, so the ring is 4 steps deep. The two M=128 x
-// N=bn accumulators fill most of TMEM, so the epilogue does not overlap the
-// next tile's MMAs; 8 epilogue warps keep that drain short. bn below 224 only
-// serves to round the tile count to whole waves of CTAs.
+// What bounds it on B200: shared-memory traffic. Per 64-K step a CTA writes the
+// x tile (TMA) and the dequantised B tile, and the tensor core reads x once and
+// B twice (once per 128-row half) -- ~150 KB per step against ~90 B/clk per SM,
+// the rate a cuBLAS bf16 GEMM at 1.63 PF implies. Wider tiles amortise the x
+// tile; the packed weights bypass shared memory. Under load a TMA load takes
+// ~1.5 us to land, so the x ring is 5 steps deep. The two M=128 x N=bn
+// accumulators fill most of TMEM, so the epilogue does not overlap the next
+// tile's MMAs; 8 epilogue warps keep that drain short. bn below 224 only serves
+// to round the tile count to whole waves of CTAs.
 //
 //   warp 0       TMA producer: per step the x tile [256 x 64] fp16 (128-byte
-//                swizzle), the packed qweight tile [8 x bn] int32 and the
-//                step's scale and zero rows [bn] fp16 into a 4-deep ring, all
-//                on one transaction-counted mbarrier.
-//   warps 2..17  dequantisers: two threads per tile column each unpack 4 of the
-//                column's 8 words of the step (PRMT + LOP3 magic-number nibble
+//                swizzle) into a 5-deep ring on a transaction-counted mbarrier.
+//   warps 2..17  dequantisers: two threads per tile column each load 4 of the
+//                column's 8 packed words of the step and its scale and zero
+//                straight from global memory (L2-resident, two steps ahead),
+//                unpack them (PRMT + LOP3 magic-number nibble
 //                extraction, exact (q - z), one fp16 multiply by s: the
 //                reference's rounding) and writes the fp16 weights K-major into
 //                a 128-byte-swizzled B tile of a 2-deep ring, then
@@ -51,12 +52,10 @@ constexpr int BMH = 128;
 constexpr int BN_MAX = 224;                  // tile columns: runtime bn in [128, 224], bn % 32 == 0
 constexpr int BN_MIN = 128;
 constexpr int BK = 64;
-constexpr int TSTAGES = 4;                   // TMA ring depth (covers ~1.5 us TMA latency under load)
+constexpr int TSTAGES = 5;                   // x-tile ring depth (covers ~1.5 us TMA latency under load)
 constexpr int BSTAGES = 2;                   // dequantised-B ring depth
 constexpr int A_BYTES = BM * BK * 2;         // 32768
-constexpr int P_BYTES = (BK / 8) * BN_MAX * 4;   // 7168 (room for bn = 224)
-constexpr int SZ_BYTES = 512;                // one row of bn <= 224 fp16, padded: TMA destinations are 128-byte aligned
-constexpr int T_BYTES = A_BYTES + P_BYTES + 2 * SZ_BYTES;   // 40960 = 40 KB
+constexpr int T_BYTES = A_BYTES;             // a TMA stage holds the x tile only
 constexpr int B_BYTES = BN_MAX * BK * 2;     // 28672
 constexpr int DQ_WARPS = 16;                 // two threads per tile column, 4 words each (256 columns of room)
 constexpr int EPI_WARPS = 8;                 // two per TMEM lane quarter
@@ -70,15 +69,12 @@ constexpr int SMEM_BYTES = 1024 + TSTAGES * T_BYTES + BSTAGES * B_BYTES + BAR_BY
 static_assert(T_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(DQ_WARPS * 32 >= 2 * BN_MAX, "two dequantiser threads per tile column");
-static_assert(SZ_BYTES >= BN_MAX * 2, "scale/zero row slot");
-static_assert(A_BYTES % 128 == 0 && (A_BYTES + P_BYTES) % 128 == 0 &&
-                  (A_BYTES + P_BYTES + SZ_BYTES) % 128 == 0,
-              "every TMA destination in a stage must be 128-byte aligned");
 
-// TMA transaction bytes of one K step for a bn-column tile.
-__host__ __device__ constexpr int tx_bytes(int bn) { return A_BYTES + (BK / 8) * bn * 4 + 2 * bn * 2; }
 
 struct Params {
+  const int32_t* qw;       // packed weights [K/8, N], read by the dequantisers with plain loads
+  const __half* scales;    // [K/G, N]
+  const __half* zeros;     // [K/G, N]
   const __half* bias;
   void* y;         // fp16, or fp32 when y_f32 (unrounded partial sums, no bias)
   int y_f32;
@@ -130,14 +126,11 @@ struct Ring {
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
-    w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x,
-                         const __grid_constant__ CUtensorMap tm_p,
-                         const __grid_constant__ CUtensorMap tm_s,
-                         const __grid_constant__ CUtensorMap tm_z, const Params p) {
+    w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* tring = smem;                                   // TSTAGES x {A, P, S, Z}
+  uint8_t* tring = smem;                                   // TSTAGES x x tile
   uint8_t* bring = smem + TSTAGES * T_BYTES;               // BSTAGES x B
   uint64_t* bars = reinterpret_cast<uint64_t*>(bring + BSTAGES * B_BYTES);
   uint64_t* tfull = bars;
@@ -182,26 +175,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------ TMA producer --------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tm_x);
-      tma_prefetch_desc(&tm_p);
-      tma_prefetch_desc(&tm_s);
-      tma_prefetch_desc(&tm_z);
-      const uint32_t tx = static_cast<uint32_t>(tx_bytes(bn));
       Ring r;
       long long issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
         const int m0 = (tile % p.m_tiles) * BM;
-        const int n0 = (tile / p.m_tiles) * bn;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u)) { ok = false; break; }
           uint8_t* st = tring + r.slot * T_BYTES;
-          const int kk = kt * BK;
-          const int grow = p.g_shift >= 0 ? kk >> p.g_shift : kk / p.G;
-          mbar_arrive_expect_tx(&tfull[r.slot], tx);
-          tma_load_2d(st, &tm_x, &tfull[r.slot], kk, m0);
-          tma_load_2d(st + A_BYTES, &tm_p, &tfull[r.slot], n0, kt * (BK / 8));
-          tma_load_2d(st + A_BYTES + P_BYTES, &tm_s, &tfull[r.slot], n0, grow);
-          tma_load_2d(st + A_BYTES + P_BYTES + SZ_BYTES, &tm_z, &tfull[r.slot], n0, grow);
+          mbar_arrive_expect_tx(&tfull[r.slot], A_BYTES);
+          tma_load_2d(st, &tm_x, &tfull[r.slot], kt * BK, m0);
           r.advance(TSTAGES);
           ++issued;
         }
@@ -253,42 +236,65 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp < EPI_WARP0) {
     // ------------------------------ dequantisers --------------------------
+    // The packed words and the scale/zero of a step come straight from global
+    // memory (L2-resident: every m-tile re-reads the n-tile's weights), loaded two
+    // steps ahead into registers; only the dequantised B tile goes through shared
+    // memory, which is what bounds this kernel.
     const int dt = threadIdx.x - 64;
     const int t = dt & 255;              // column of the tile owned by this thread
     const int c0 = (dt >> 8) * 4;        // its 4 words (32 K) of the step's 8
     const bool active = t < bn;
-    Ring tr, br;
+    const long long ldq = p.N;
+    Ring br;
     bool ok = true;
+    struct Step {
+      uint32_t w[4];
+      uint32_t s, z;
+    };
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+      const int n = (tile / p.m_tiles) * bn + t;
+      const bool colok = active && n < p.N;
+      auto fetch = [&](int kt, Step& f) {
+        if (colok && kt < KT) {
+          const int32_t* wp = p.qw + (static_cast<long long>(kt) * 8 + c0) * ldq + n;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) f.w[c] = ldg_nc_u32(wp + c * ldq);
+          const int kk = kt * BK;
+          const long long grow = p.g_shift >= 0 ? kk >> p.g_shift : kk / p.G;
+          f.s = ldg_nc_u16(p.scales + grow * ldq + n);
+          f.z = ldg_nc_u16(p.zeros + grow * ldq + n);
+        } else {
+          f.w[0] = f.w[1] = f.w[2] = f.w[3] = 0u;
+          f.s = f.z = 0u;
+        }
+      };
+      Step cur, nxt, nnx;
+      fetch(0, cur);
+      fetch(1, nxt);
       for (int kt = 0; kt < KT; ++kt) {
-        if (!warp_wait(&tfull[tr.slot], tr.phase) || !warp_wait(&bempty[br.slot], br.phase ^ 1u)) {
+        fetch(kt + 2, nnx);
+        if (!warp_wait(&bempty[br.slot], br.phase ^ 1u)) {
           ok = false;
           break;
         }
         if (active) {
-          const uint8_t* st = tring + tr.slot * T_BYTES;
-          const __half sv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES)[t];
-          const __half zv = reinterpret_cast<const __half*>(st + A_BYTES + P_BYTES + SZ_BYTES)[t];
-          const uint32_t ss = static_cast<uint32_t>(__half_as_ushort(sv)) * 0x10001u;
+          const uint32_t ss = cur.s * 0x10001u;
+          const __half zv = __ushort_as_half(static_cast<unsigned short>(cur.z));
           const uint32_t zc =
               static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
               (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
-          // the packed tile is [8 rows x bn] int32, row-major
-          const uint32_t* pk = reinterpret_cast<const uint32_t*>(st + A_BYTES);
-          uint32_t w[4];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) w[c] = pk[(c0 + c) * bn + t];
           uint8_t* brow = bring + br.slot * B_BYTES + t * 128;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) = dequant_word_nat(w[c], zc, ss);
+            *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) = dequant_word_nat(cur.w[c], zc, ss);
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bfull[br.slot]);
-        tr.advance(TSTAGES);
         br.advance(BSTAGES);
+        cur = nxt;
+        nxt = nnx;
       }
     }
   } else {

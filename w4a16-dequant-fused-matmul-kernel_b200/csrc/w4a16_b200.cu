@@ -281,9 +281,9 @@ int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, 
 
 // Tile width of the prefill kernel for this shape: the candidate with the least
 // modelled time = waves of tiles x cycles per K step, where a step costs the
-// larger of its MMAs (4 * bn cycles) and its L2 traffic (x tile 32 KB + 36 B per
-// column at ~31.5 B/clk per SM, measured on B200). Wider tiles reuse the x
-// tile more; narrower ones can round the tile count to whole waves.
+// larger of its MMAs (4 * bn cycles) and its operand traffic (x tile 32 KB plus
+// a per-column share, at the ~32 B/clk per SM measured on B200). Wider tiles
+// reuse the x tile more; narrower ones can round the tile count to whole waves.
 int choose_prefill_bn(int M, int N, int num_sms) {
   const long long m_tiles = (M + prefill::BM - 1) / prefill::BM;
   int best = prefill::BN_MAX;
@@ -305,18 +305,15 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
                    const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                    long long ldy, cudaStream_t stream) {
   const int bn = choose_prefill_bn(M, N, dev.num_sms);
-  CUtensorMap tx, tp, ts, tz;
+  CUtensorMap tx;
   if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map_2d(&tp, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, qw, N, K / 8, N, bn,
-                   prefill::BK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, N, K / G, N, bn, 1,
-                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, z, N, K / G, N, bn, 1,
-                   CU_TENSOR_MAP_SWIZZLE_NONE)) {
+                   CU_TENSOR_MAP_SWIZZLE_128B)) {
     return W4A16_ERR_ALIGNMENT;
   }
   prefill::Params p;
+  p.qw = qw;
+  p.scales = s;
+  p.zeros = z;
   p.bias = bias;
   p.y = y;
   p.y_f32 = y_f32;
@@ -333,8 +330,7 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.vec_store = (aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0) ? 1 : 0;
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
-  prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, tp, ts,
-                                                                                       tz, p);
+  prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, p);
   W4A16_RETURN_IF_LAUNCH_FAILED();
   return W4A16_OK;
 }
