@@ -227,3 +227,27 @@ def test_decode_and_prefill_routes_agree():
     parts = torch.cat([w4a16_matmul(X[i:i + 32].contiguous(), qw, s, z, 128) for i in range(0, 96, 32)])
     assert_gemm_close(np_(parts), np_(full), "decode vs prefill")
     assert_gemm_close(np_(full), np_(torch_reference(X, qw, s, z, 128)), "vs torch fp32")
+
+
+@pytest.mark.parametrize("M", [5, 300])
+@pytest.mark.parametrize("pad", [0, 8, 3])
+def test_column_slices_of_a_wider_output(M, pad):
+    """Two column shards written into one [M, 2N + pad] buffer through the row-pitch
+    argument (decode and prefill routes; pitches that allow TMA stores and one that
+    does not). Every element outside the shards keeps its sentinel value."""
+    from w4a16.gemm import w4a16_matmul_into
+    K, N, G = 1024, 264, 128
+    X, W = gpu_case(M, K, 2 * N, G, sigma=0.05, seed=7 + M)
+    qw, s, z = quantize_weight(W, G)
+    full = w4a16_matmul(X, qw, s, z, G)
+    ldy = 2 * N + pad
+    buf = torch.full((M, ldy), 7.0, device="cuda", dtype=torch.float16)
+    for r in range(2):
+        sl = slice(r * N, (r + 1) * N)
+        w4a16_matmul_into(X, qw[:, sl].contiguous(), s[:, sl].contiguous(), z[:, sl].contiguous(), G,
+                          buf[:, sl], ldy)
+    torch.cuda.synchronize()
+    # (stream-K split points depend on N, so the fp32 summation order may differ)
+    assert_gemm_close(np_(buf[:, :2 * N]), np_(full).astype(np.float32), "column slices")
+    if pad:
+        assert torch.all(buf[:, 2 * N:] == 7.0), "a store landed outside the shards"

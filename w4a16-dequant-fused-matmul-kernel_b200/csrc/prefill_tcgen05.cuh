@@ -35,7 +35,9 @@
 //   warps 18..25 epilogue: two warps per 32-lane TMEM quarter (one per 128-row
 //                half) read the accumulators with tcgen05.ld, round to fp16,
 //                add the optional bias (rounded again, as W4A16Linear's separate
-//                add does) and store.
+//                add does), stage each 32 x 32 chunk in a swizzled shared-memory
+//                tile and write it with a TMA tensor store (plain stores when y is
+//                not 16-byte aligned).
 //
 // Every mbarrier wait is bounded; on expiry the role raises the sticky device
 // error bit and leaves its loops, the producer drains its in-flight copies,
@@ -52,7 +54,7 @@ constexpr int BMH = 128;
 constexpr int BN_MAX = 224;                  // tile columns: runtime bn in [128, 224], bn % 32 == 0
 constexpr int BN_MIN = 128;
 constexpr int BK = 64;
-constexpr int TSTAGES = 5;                   // x-tile ring depth (covers ~1.5 us TMA latency under load)
+constexpr int TSTAGES = 4;                   // x-tile ring depth (covers ~1.5 us TMA latency under load)
 constexpr int BSTAGES = 2;                   // dequantised-B ring depth
 constexpr int A_BYTES = BM * BK * 2;         // 32768
 constexpr int T_BYTES = A_BYTES;             // a TMA stage holds the x tile only
@@ -63,8 +65,10 @@ constexpr int NUM_WARPS = 2 + DQ_WARPS + EPI_WARPS;
 constexpr int THREADS = NUM_WARPS * 32;
 constexpr int EPI_WARP0 = 2 + DQ_WARPS;
 constexpr uint32_t TMEM_COLS = 512;          // two 128-row halves x bn columns (bn <= 224)
+constexpr int STG_BYTES = 4096;              // per epilogue warp: a 32 x 32 output chunk (fp32 at most)
 constexpr int BAR_BYTES = 256;
-constexpr int SMEM_BYTES = 1024 + TSTAGES * T_BYTES + BSTAGES * B_BYTES + BAR_BYTES;
+constexpr int SMEM_BYTES =
+    1024 + TSTAGES * T_BYTES + BSTAGES * B_BYTES + EPI_WARPS * STG_BYTES + BAR_BYTES;
 
 static_assert(T_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must keep 1024-byte alignment");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -72,6 +76,7 @@ static_assert(DQ_WARPS * 32 >= 2 * BN_MAX, "two dequantiser threads per tile col
 
 
 struct Params {
+  int tma_store;           // y written by TMA stores from a staging tile (y 16-byte aligned, ldy % 8 / % 4 == 0)
   const int32_t* qw;       // packed weights [K/8, N], read by the dequantisers with plain loads
   const __half* scales;    // [K/G, N]
   const __half* zeros;     // [K/G, N]
@@ -126,13 +131,15 @@ struct Ring {
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
-    w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const Params p) {
+    w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
+                         const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* tring = smem;                                   // TSTAGES x x tile
   uint8_t* bring = smem + TSTAGES * T_BYTES;               // BSTAGES x B
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + BSTAGES * B_BYTES);
+  uint8_t* staging = bring + BSTAGES * B_BYTES;            // EPI_WARPS x STG_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + EPI_WARPS * STG_BYTES);
   uint64_t* tfull = bars;
   uint64_t* tempty = tfull + TSTAGES;
   uint64_t* bfull = tempty + TSTAGES;
@@ -301,17 +308,61 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------ epilogue -------------------------------
     const int quarter = warp & 3;                 // TMEM lanes this warp may access
     const int h = (warp - EPI_WARP0) >> 2;        // 128-row half of the tile
+    uint8_t* stg = staging + (warp - EPI_WARP0) * STG_BYTES;
+    if (p.tma_store && lane == 0) tma_prefetch_desc(&tm_y);
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       if (!warp_wait(accfull, local & 1)) break;
       tc_fence_after();
       const int n0 = (tile / p.m_tiles) * bn;
-      const int m = (tile % p.m_tiles) * BM + h * BMH + quarter * 32 + lane;
+      const int mrow0 = (tile % p.m_tiles) * BM + h * BMH + quarter * 32;
+      const int m = mrow0 + lane;
 #pragma unroll 1
       for (int col = 0; col < bn; col += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + h * bn + col + (static_cast<uint32_t>(quarter * 32) << 16), r);
         tmem_ld_wait();
+        if (p.tma_store) {
+          // Stage the warp's 32 x 32 chunk (row = lane) in the TMA swizzle layout and
+          // store it with one bulk tensor copy; rows >= M and columns >= N are clipped.
+          if (lane == 0) bulk_wait_group_read0();   // the previous chunk has left the buffer
+          __syncwarp();
+          if (p.y_f32) {
+            // 128-byte rows, 128-byte swizzle: 16-byte chunk c at c ^ (row & 7)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                  make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+          } else {
+            uint32_t packed[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              __half lo = __float2half_rn(__uint_as_float(r[2 * e]));
+              __half hi = __float2half_rn(__uint_as_float(r[2 * e + 1]));
+              if (p.bias != nullptr) {
+                const int nb = n0 + col + 2 * e;
+                const float blo = nb < p.N ? __half2float(p.bias[nb]) : 0.0f;
+                const float bhi = nb + 1 < p.N ? __half2float(p.bias[nb + 1]) : 0.0f;
+                lo = __float2half_rn(__half2float(lo) + blo);
+                hi = __float2half_rn(__half2float(hi) + bhi);
+              }
+              packed[e] = static_cast<uint32_t>(__half_as_ushort(lo)) |
+                          (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+            }
+            // 64-byte rows, 64-byte swizzle: 16-byte chunk c at c ^ ((row >> 1) & 3)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+                  make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && mrow0 < p.M && n0 + col < p.N) {
+            tma_store_2d(&tm_y, stg, n0 + col, mrow0);
+            bulk_commit_group();
+          }
+          continue;
+        }
         if (m < p.M && p.y_f32) {
           float* yrow = static_cast<float*>(p.y) + static_cast<long long>(m) * p.ldy + n0 + col;
 #pragma unroll
@@ -359,6 +410,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty);
     }
+    if (p.tma_store && lane == 0) bulk_wait_group0();   // every store of this warp has landed
   }
 
   tc_fence_before();

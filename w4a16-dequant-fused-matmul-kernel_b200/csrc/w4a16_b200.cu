@@ -305,12 +305,22 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
                    const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                    long long ldy, cudaStream_t stream) {
   const int bn = choose_prefill_bn(M, N, dev.num_sms);
-  CUtensorMap tx;
+  CUtensorMap tx, ty;
   if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
                    CU_TENSOR_MAP_SWIZZLE_128B)) {
     return W4A16_ERR_ALIGNMENT;
   }
+  // y through TMA stores when its base and row pitch are 16-byte aligned: 32 x 32
+  // boxes, fp16 rows of 64 B (64-byte swizzle) or fp32 rows of 128 B (128-byte swizzle).
+  const bool y_aligned = aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0;
+  const bool tma_store =
+      y_aligned && (y_f32 ? make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, N, M, ldy, 32, 32,
+                                        CU_TENSOR_MAP_SWIZZLE_128B)
+                          : make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y, N, M, ldy, 32, 32,
+                                        CU_TENSOR_MAP_SWIZZLE_64B));
+  if (!tma_store) ty = tx;   // unused by the kernel
   prefill::Params p;
+  p.tma_store = tma_store ? 1 : 0;
   p.qw = qw;
   p.scales = s;
   p.zeros = z;
@@ -330,7 +340,7 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.vec_store = (aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0) ? 1 : 0;
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
-  prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, p);
+  prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
   W4A16_RETURN_IF_LAUNCH_FAILED();
   return W4A16_OK;
 }
