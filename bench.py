@@ -566,6 +566,8 @@ def run_mlp(args):
         for ln in lines:
             print(json.dumps(ln), flush=True)
     if world > 1:
+        from w4a16.parallel import close_peer_channels
+        close_peer_channels()   # collective; before the process group goes away
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -7,7 +7,8 @@
  * entry point returns 0 on success or a negative W4A16_* status, and
  * w4a16_strerror() turns a status into text. All launches are asynchronous
  * on the given stream; nothing here allocates device memory or synchronises
- * (scratch memory, where a kernel needs it, is passed in by the caller).
+ * (scratch memory, where a kernel needs it, is passed in by the caller) except
+ * the peer-to-peer buffer helpers w4a16_p2p_*, which set up the multi-GPU path.
  *
  * Data format (the reference's, unchanged): W is [K, N] (K = in_features),
  * quantised in groups of G consecutive K-rows per column.
@@ -179,6 +180,45 @@ int w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales
                        const void* zeros, const void* bias, void* y,
                        int64_t M, int64_t N, int64_t K, int64_t group_size,
                        int64_t ldy, void* stream);
+
+/*
+ * Row-parallel decode GEMM fused with its all-reduce (no counterpart in the
+ * reference, which has no multi-GPU path): y = fp16(sum over the `world` ranks of
+ * x_r @ dequant(W_r)) [+ bias, rounded again], where each rank holds a K-slice
+ * of x and of the weight. One kernel per rank: its CTAs write their fp32 partial
+ * sums straight into this rank's slot of every rank's peer-to-peer buffer (plain
+ * stores over NVLink); the CTA that finishes last raises this rank's flag in
+ * every buffer, waits (bounded) for every rank's flag in its own buffer, and sums
+ * the slots in rank order into y -- the same values as an fp32 all-reduce of the
+ * partials followed by one fp16 rounding.
+ *
+ * peers: device array of `world` buffer addresses as mapped on this GPU (this
+ * rank's own buffer at index `rank`), each w4a16_p2p_buffer_bytes(world, slot)
+ * bytes, zeroed before first use (w4a16_p2p_alloc does). ctl: this rank's two
+ * device int32 control words, zeroed before first use. slot >= M * N. Every rank
+ * must issue the same sequence of calls on one stream (a call's flags and data
+ * alternate between two buffer halves by the call count kept in ctl); calls on a
+ * buffer must not overlap. Requirements as w4a16_gemm plus M <= 32, N % 8 == 0,
+ * 16-byte-aligned inputs, 2 <= world <= 8. The workspace is w4a16_gemm's.
+ */
+int w4a16_gemm_allreduce(const void* x, const int32_t* qweight, const void* scales,
+                         const void* zeros, const void* bias, void* y,
+                         int64_t M, int64_t N, int64_t K, int64_t group_size,
+                         int64_t ldy, void* workspace, int64_t workspace_bytes,
+                         const unsigned long long* peers, int world, int rank,
+                         int* ctl, int64_t slot, void* stream);
+
+/* Bytes of one rank's peer-to-peer buffer for w4a16_gemm_allreduce. */
+int w4a16_p2p_buffer_bytes(int world, int64_t slot, int64_t* bytes_out);
+
+/* A zeroed device buffer of `bytes` on the current device and its 64-byte CUDA
+ * IPC handle (for the peers' w4a16_p2p_open); release with w4a16_p2p_free. */
+int w4a16_p2p_alloc(int64_t bytes, void** ptr_out, void* handle_out);
+
+/* Map a peer's buffer from its 64-byte IPC handle; release with w4a16_p2p_close. */
+int w4a16_p2p_open(const void* handle, void** ptr_out);
+int w4a16_p2p_close(void* ptr);
+int w4a16_p2p_free(void* ptr);
 
 #ifdef __cplusplus
 }

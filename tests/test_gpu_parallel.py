@@ -137,3 +137,90 @@ def test_two_gpu_column_gather_and_mlp():
     ref = _mlp_oracle(X, quantize_weight(Wg, G), quantize_weight(Wu, G), quantize_weight(Wd, G), G)
     for rank, _, y, _ in res:
         assert_gemm_close(y, ref, f"tp mlp rank {rank}")
+
+
+def _fused_row_rank(rank: int, world: int, port: int, q) -> None:
+    try:
+        for p in (os.path.join(ROOT, "w4a16-dequant-fused-matmul-kernel_b200"), ROOT,
+                  os.path.join(ROOT, "tests")):
+            sys.path.insert(0, p)
+        import datetime
+        import torch.distributed as dist
+        from helpers import gpu_case as case
+        from w4a16 import _lib, quantize_weight as quant
+        from w4a16.parallel import RowParallelW4A16Linear as Row, close_peer_channels
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        K, N, G = 2048, 1024, 128
+        results = {}
+        for M in (1, 5, 32):
+            X, Wd = case(M, K, N, G, sigma=0.05, seed=11 + M, device=dev)
+            qd = quant(Wd, G)
+            bias = (torch.randn(N, generator=torch.Generator(device=dev).manual_seed(3), device=dev)
+                    * 0.1).half()
+            for use_bias in (False, True):
+                fused = Row.from_quantized(*qd, G, bias=bias if use_bias else None)
+                nccl = Row.from_quantized(*qd, G, bias=bias if use_bias else None)
+                nccl.fused_allreduce = False
+                k = K // world
+                xl = X[:, rank * k:(rank + 1) * k].contiguous()
+                outs = [fused(xl) for _ in range(3)]           # several epochs: both halves
+                ref = nccl(xl)
+                results[(M, use_bias)] = (np_(torch.stack(outs)), np_(ref))
+        # the fused call inside a CUDA graph, replayed (the epoch lives on the device)
+        M = 1
+        X, Wd = case(M, K, N, G, sigma=0.05, seed=99, device=dev)
+        qd = quant(Wd, G)
+        row = Row.from_quantized(*qd, G)
+        k = K // world
+        xl = X[:, rank * k:(rank + 1) * k].contiguous()
+        eager = row(xl)
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            row(xl)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                yg = row(xl)
+            for _ in range(4):
+                g.replay()
+        torch.cuda.synchronize(dev)
+        graph_ok = bool(torch.equal(yg, eager))
+        flags = _lib.check_device_errors(dev)
+        del g
+        close_peer_channels()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, results, graph_ok, flags, None))
+    except Exception as e:
+        import traceback
+        q.put((rank, None, None, None, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_fused_row_parallel_gemm_allreduce():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_row_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for rank, results, graph_ok, flags, err in res:
+        assert err is None, f"rank {rank}: {err}"
+        assert flags == 0, f"rank {rank}: device error flags {flags}"
+        assert graph_ok, f"rank {rank}: graph replays differ from the eager fused call"
+        for (M, use_bias), (outs, ref) in results.items():
+            for i in range(outs.shape[0]):
+                # same partials, same fp32 sum (two terms commute), one fp16 rounding
+                assert np.array_equal(outs[i], ref), f"rank {rank} M={M} bias={use_bias} call {i}"
+    # the ranks agree with each other
+    for key in res[0][1]:
+        assert np.array_equal(res[0][1][key][0], res[1][1][key][0])

@@ -89,7 +89,27 @@ struct Params {
   int kstages;            // K stages per strip (ceil(K / 512))
   long long units;        // strips * kstages
   int num_stages;         // ring depth
+  // Fused all-reduce (ar_world > 1): this rank's y is the sum over ranks of every
+  // rank's partial GEMM (a row-parallel layer). Each rank owns one peer-to-peer
+  // buffer (layout below); ar_peers[q] is rank q's buffer as mapped on this GPU.
+  int ar_world, ar_rank;
+  const unsigned long long* ar_peers;   // device array [ar_world]
+  int* ar_ctl;                          // this rank's control words: [0] epoch, [1] CTAs finished
+  long long ar_slot;                    // fp32 elements per rank slot (>= M * N)
 };
+
+// Peer-to-peer all-reduce buffer (one per rank): two halves, selected by the
+// epoch's parity, each with a flag per rank and a data slot per rank.
+//   [flags: 2 x AR_MAX_RANKS u32][pad to AR_DATA_OFF][data: 2 x world x slot fp32]
+// A rank writes its partial into its own slot of every rank's buffer, then the
+// epoch + 1 into its own flag of every rank's buffer. A rank can only be one
+// epoch ahead of another (it needs everyone's flag of the previous epoch before
+// its next launch), so the half it writes is never the one a peer still reads.
+constexpr int AR_MAX_RANKS = 8;
+constexpr long long AR_DATA_OFF = 256;   // bytes
+__host__ __device__ constexpr long long ar_buffer_bytes(int world, long long slot) {
+  return AR_DATA_OFF + 2ll * world * slot * 4;
+}
 
 // c (+)= a * b on the tensor core, m16n8k16, fp16 in, fp32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -136,7 +156,13 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
 }
 
-__device__ __forceinline__ void emit(const Params& p, int t, int n, float v) {
+__device__ __forceinline__ void emit(const Params& p, int t, int n, float v, long long ar_off) {
+  if (p.ar_world > 1) {
+    // the unrounded partial into this rank's slot of its own buffer; the last CTA
+    // pushes the whole slot to the peers
+    reinterpret_cast<float*>(p.ar_peers[p.ar_rank])[ar_off + static_cast<long long>(t) * p.N + n] = v;
+    return;
+  }
   const long long o = static_cast<long long>(t) * p.ldy + n;
   if (p.y_f32) {
     static_cast<float*>(p.y)[o] = v;
@@ -276,6 +302,15 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     return;   // takes no part in the consumers' barriers below
   }
   pdl_wait();   // x, y and the workspace are only touched after the previous kernel
+
+  // Fused all-reduce: this launch's epoch (the previous launch on this stream has
+  // completed, so its epoch advance is visible) and this rank's slot in the half.
+  int ar_epoch = 0;
+  long long ar_off = 0;
+  if (p.ar_world > 1) {
+    ar_epoch = *reinterpret_cast<volatile int*>(p.ar_ctl);
+    ar_off = AR_DATA_OFF / 4 + (static_cast<long long>(ar_epoch & 1) * p.ar_world + p.ar_rank) * p.ar_slot;
+  }
 
   // -------------------------------- consumers ---------------------------------
   const int cw = warp - 1;
@@ -426,7 +461,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
 #pragma unroll
           for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
           const int n = c * BN + cc;
-          if (n < p.N) emit(p, t, n, v);
+          if (n < p.N) emit(p, t, n, v, ar_off);
         }
       } else if (u != u1 - 1) {
         // the first strip, split and not the final segment: park its piece (slot 0)
@@ -493,7 +528,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
         for (int i = 0; i < MAXP; ++i) v += part[i];
       }
       const int n = cs * BN + cc;
-      if (n < p.N) emit(p, t, n, v);
+      if (n < p.N) emit(p, t, n, v, ar_off);
     }
   };
 
@@ -551,6 +586,76 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
       __threadfence();
       if (ctid == 0) p.counters[c_first] = 0u;
       sum_strip(c_first, false);
+    }
+  }
+
+  if (p.ar_world > 1) {
+    // ---------- fused all-reduce: the last CTA of this rank finishes the call ----------
+    consumer_sync<NCW>();
+    if (ctid == 0) {
+      __threadfence();   // this CTA's partials before its count
+      flag[3] = atomicAdd(p.ar_ctl + 1, 1) == static_cast<int>(gridDim.x) - 1 ? 1 : 0;
+    }
+    consumer_sync<NCW>();
+    if (flag[3]) {
+      __threadfence();   // every CTA's partials (counted above) are visible to this CTA
+      const int half = ar_epoch & 1;
+      const unsigned tag = static_cast<unsigned>(ar_epoch) + 1u;
+      const int total = M * p.N;   // N % 8 == 0: whole float4s
+      const float* mine = reinterpret_cast<const float*>(p.ar_peers[p.ar_rank]) + ar_off;
+      // push this rank's slot into every peer's buffer (vector stores over NVLink)
+      for (int q = 0; q < p.ar_world; ++q) {
+        if (q == p.ar_rank) continue;
+        float* dst = reinterpret_cast<float*>(p.ar_peers[q]) + ar_off;
+        for (int i = ctid * 4; i < total; i += NCW * 32 * 4)
+          *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(mine + i));
+      }
+      consumer_sync<NCW>();
+      if (ctid == 0) {
+        __threadfence_system();   // the pushed slots before the flags
+        p.ar_ctl[1] = 0;   // the next launch counts from zero
+        for (int q = 0; q < p.ar_world; ++q) {
+          unsigned* f = reinterpret_cast<unsigned*>(p.ar_peers[q]) + half * AR_MAX_RANKS + p.ar_rank;
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(tag) : "memory");
+        }
+      }
+      // every rank's flag in this rank's own buffer (bounded wait)
+      if (ctid < p.ar_world) {
+        const unsigned* f = reinterpret_cast<const unsigned*>(p.ar_peers[p.ar_rank]) + half * AR_MAX_RANKS + ctid;
+        const uint64_t t0 = global_timer_ns();
+        for (uint32_t i = 0;; ++i) {
+          unsigned v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+          if (v == tag) break;
+          if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitBudgetNs) {
+            flag_error(kErrWaitTimeout);
+            break;
+          }
+        }
+      }
+      consumer_sync<NCW>();
+      // y = fp16(sum of the ranks' partials, in rank order) [+ bias, rounded again]
+      const float* own = reinterpret_cast<const float*>(p.ar_peers[p.ar_rank]) + AR_DATA_OFF / 4 +
+                         static_cast<long long>(half) * p.ar_world * p.ar_slot;
+      for (int i = ctid * 4; i < total; i += NCW * 32 * 4) {
+        float4 v = __ldcg(reinterpret_cast<const float4*>(own + i));
+        for (int q = 1; q < p.ar_world; ++q) {
+          const float4 w = __ldcg(reinterpret_cast<const float4*>(own + q * p.ar_slot + i));
+          v.x += w.x;
+          v.y += w.y;
+          v.z += w.z;
+          v.w += w.w;
+        }
+        const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int idx = i + j, t = idx / p.N, n = idx - t * p.N;
+          __half h = __float2half_rn(e[j]);
+          if (p.bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(p.bias[n]));
+          static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + n] = h;
+        }
+      }
+      if (ctid == 0) p.ar_ctl[0] = ar_epoch + 1;   // the next launch's epoch
     }
   }
 }

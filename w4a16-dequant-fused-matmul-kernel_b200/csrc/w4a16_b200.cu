@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -203,10 +204,18 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   return W4A16_OK;
 }
 
+// Fused all-reduce arguments of the decode kernel (world 0: off).
+struct ArArgs {
+  int world = 0, rank = 0;
+  const unsigned long long* peers = nullptr;
+  int* ctl = nullptr;
+  long long slot = 0;
+};
+
 int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                       const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                       long long ldy, void* workspace, int64_t workspace_bytes,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const ArArgs& ar = ArArgs()) {
   DecodePlan d;
   int st = plan_decode(dev, M, N, K, &d);
   if (st != W4A16_OK) return st;
@@ -239,6 +248,11 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.kstages = d.kstages;
   p.units = d.units;
   p.num_stages = d.nst;
+  p.ar_world = ar.world;
+  p.ar_rank = ar.rank;
+  p.ar_peers = ar.peers;
+  p.ar_ctl = ar.ctl;
+  p.ar_slot = ar.slot;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(d.grid), 1, 1);
@@ -665,4 +679,98 @@ extern "C" int w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const v
   if (st != W4A16_OK) return st;
   return gemm_impl(x, qweight, scales, zeros, bias, y, 0, M, N, K, group_size, ldy, scratch,
                    W4A16_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Row-parallel decode GEMM fused with its all-reduce over NVLink peer memory
+// ---------------------------------------------------------------------------
+extern "C" int w4a16_gemm_allreduce(const void* x, const int32_t* qweight, const void* scales,
+                                    const void* zeros, const void* bias, void* y, int64_t M, int64_t N,
+                                    int64_t K, int64_t group_size, int64_t ldy, void* workspace,
+                                    int64_t workspace_bytes, const unsigned long long* peers,
+                                    int world, int rank, int* ctl, int64_t slot, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
+  if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
+  if (ldy < N || M > 32 || N % 8 != 0) return W4A16_ERR_INVALID;
+  if (world < 2 || world > decode::AR_MAX_RANKS || rank < 0 || rank >= world) return W4A16_ERR_INVALID;
+  if (peers == nullptr || ctl == nullptr || slot < M * N) return W4A16_ERR_INVALID;
+  if (M == 0 || N == 0) return W4A16_OK;
+  if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || y == nullptr)
+    return W4A16_ERR_INVALID;
+  if (N > (1ll << 30) || K > (1ll << 30) || (N + decode::BN - 1) / decode::BN > decode::MAX_STRIPS)
+    return W4A16_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales) || !aligned16(zeros))
+    return W4A16_ERR_ALIGNMENT;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  ArArgs ar;
+  ar.world = world;
+  ar.rank = rank;
+  ar.peers = peers;
+  ar.ctl = ctl;
+  ar.slot = slot;
+  return launch_decode_tma(*dev, static_cast<const __half*>(x), qweight, static_cast<const __half*>(scales),
+                           static_cast<const __half*>(zeros), static_cast<const __half*>(bias), y, 0,
+                           static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                           static_cast<int>(group_size), ldy, workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream), ar);
+}
+
+extern "C" int w4a16_p2p_buffer_bytes(int world, int64_t slot, int64_t* bytes_out) {
+  if (bytes_out == nullptr || world < 2 || world > decode::AR_MAX_RANKS || slot <= 0)
+    return W4A16_ERR_INVALID;
+  *bytes_out = decode::ar_buffer_bytes(world, slot);
+  return W4A16_OK;
+}
+
+extern "C" int w4a16_p2p_alloc(int64_t bytes, void** ptr_out, void* handle_out) {
+  if (bytes <= 0 || ptr_out == nullptr || handle_out == nullptr) return W4A16_ERR_INVALID;
+  void* p = nullptr;
+  if (cudaMalloc(&p, static_cast<size_t>(bytes)) != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_DEVICE;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, static_cast<size_t>(bytes)) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(p);
+    return W4A16_ERR_DEVICE;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  memcpy(handle_out, &h, sizeof(h));
+  *ptr_out = p;
+  return W4A16_OK;
+}
+
+extern "C" int w4a16_p2p_open(const void* handle, void** ptr_out) {
+  if (handle == nullptr || ptr_out == nullptr) return W4A16_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_DEVICE;
+  }
+  *ptr_out = p;
+  return W4A16_OK;
+}
+
+extern "C" int w4a16_p2p_close(void* ptr) {
+  if (ptr == nullptr) return W4A16_ERR_INVALID;
+  if (cudaIpcCloseMemHandle(ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_DEVICE;
+  }
+  return W4A16_OK;
+}
+
+extern "C" int w4a16_p2p_free(void* ptr) {
+  if (ptr == nullptr) return W4A16_ERR_INVALID;
+  if (cudaFree(ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_DEVICE;
+  }
+  return W4A16_OK;
 }

@@ -13,7 +13,9 @@ schemes the benchmark configurations name:
   ``[r*K/p, (r+1)*K/p)`` (K/p must stay a multiple of the group size) and a
   K-slice of x. Each rank computes unrounded fp32 partial sums, they are
   all-reduced (sum) in fp32 and rounded to fp16 once, so the sharded layer
-  matches the unsharded one within the parity tolerance.
+  matches the unsharded one within the parity tolerance. Up to 32 tokens the
+  GEMM and the all-reduce run as one kernel per rank over NVLink peer memory
+  (``w4a16.p2p.PeerAllReduce``); larger inputs use NCCL.
 * ``W4A16MLP``: the decoder MLP block -- gate and up projections fused into
   one column-parallel GEMM ([gate shard | up shard] side by side), SwiGLU,
   then the row-parallel down projection and its all-reduce.
@@ -31,6 +33,7 @@ from .gemm import swiglu, w4a16_matmul, w4a16_matmul_f32
 from .quant import quantize_weight
 
 __all__ = [
+    "close_peer_channels",
     "shard_columns",
     "shard_rows",
     "gather_columns",
@@ -39,6 +42,27 @@ __all__ = [
     "RowParallelW4A16Linear",
     "W4A16MLP",
 ]
+
+
+_peer_channels: dict = {}
+
+
+def _peer_channel(group, device: torch.device, n: int):
+    """The fused GEMM + all-reduce channel for (group, device, n); created on first use
+    (collectively: every rank's first eligible forward reaches here in the same order)."""
+    from .p2p import PeerAllReduce
+    key = (id(group), device.index, n)
+    ch = _peer_channels.get(key)
+    if ch is None:
+        ch = _peer_channels[key] = PeerAllReduce(n, group=group, device=device)
+    return ch
+
+
+def close_peer_channels() -> None:
+    """Collective: release every peer channel (call before destroying the process group)."""
+    for key in sorted(_peer_channels, key=lambda k: (k[1], k[2])):
+        _peer_channels[key].close()
+    _peer_channels.clear()
 
 
 def _world(group=None) -> tuple[int, int]:
@@ -135,10 +159,11 @@ class RowParallelW4A16Linear(nn.Module):
     """W4A16 linear layer whose K rows (and input features) are split across ranks."""
 
     def __init__(self, in_features: int, out_features: int, group_size: int = 128,
-                 bias: bool = True, device=None, group=None) -> None:
+                 bias: bool = True, device=None, group=None, fused_allreduce: bool = True) -> None:
         super().__init__()
         self.group = group
         self.rank, self.world = _world(group)
+        self.fused_allreduce = fused_allreduce
         if in_features % self.world != 0:
             raise ValueError(f"in_features={in_features} must divide over {self.world} ranks")
         k = in_features // self.world
@@ -166,6 +191,12 @@ class RowParallelW4A16Linear(nn.Module):
 
     def forward(self, x_local: Tensor) -> Tensor:
         """``x_local`` is this rank's K-slice of the input, ``[M, K/p]``."""
+        from .p2p import MAX_TOKENS
+        if (self.world > 1 and self.fused_allreduce and x_local.is_cuda and x_local.dim() == 2
+                and x_local.shape[0] <= MAX_TOKENS and self.out_features % 8 == 0
+                and x_local.is_contiguous()):
+            ch = _peer_channel(self.group, x_local.device, self.out_features)
+            return ch.gemm(x_local, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias)
         part = w4a16_matmul_f32(x_local, self.qweight, self.scales, self.zeros, self.group_size)
         y = all_reduce_sum(part, self.group).to(torch.float16)
         return y + self.bias if self.bias is not None else y
