@@ -185,20 +185,22 @@ int w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales
  * Row-parallel decode GEMM fused with its all-reduce (no counterpart in the
  * reference, which has no multi-GPU path): y = fp16(sum over the `world` ranks of
  * x_r @ dequant(W_r)) [+ bias, rounded again], where each rank holds a K-slice
- * of x and of the weight. One kernel per rank: its CTAs write their fp32 partial
- * sums straight into this rank's slot of every rank's peer-to-peer buffer (plain
- * stores over NVLink); the CTA that finishes last raises this rank's flag in
- * every buffer, waits (bounded) for every rank's flag in its own buffer, and sums
- * the slots in rank order into y -- the same values as an fp32 all-reduce of the
- * partials followed by one fp16 rounding.
+ * of x and of the weight. One kernel per rank: the CTA that finalises an output
+ * element writes its fp32 partial, tagged with the call's epoch in one 64-bit
+ * word, into this rank's slot of every rank's peer-to-peer buffer (plain stores
+ * over NVLink; no fence, no flag); the last CTAs to finish read their share of
+ * the elements in every slot of their own buffer until each word carries the
+ * epoch's tag (bounded wait), and sum the slots in rank order into y -- the same
+ * values as an fp32 all-reduce of the partials followed by one fp16 rounding.
  *
- * peers: device array of `world` buffer addresses as mapped on this GPU (this
+ * peers: HOST array of `world` buffer addresses as mapped on this GPU (this
  * rank's own buffer at index `rank`), each w4a16_p2p_buffer_bytes(world, slot)
- * bytes, zeroed before first use (w4a16_p2p_alloc does). ctl: this rank's two
- * device int32 control words, zeroed before first use. slot >= M * N. Every rank
- * must issue the same sequence of calls on one stream (a call's flags and data
- * alternate between two buffer halves by the call count kept in ctl); calls on a
- * buffer must not overlap. Requirements as w4a16_gemm plus M <= 32, N % 8 == 0,
+ * bytes, 16-byte aligned, zeroed before first use (w4a16_p2p_alloc does); the
+ * addresses are copied into the launch. ctl: this rank's two device int32
+ * control words, zeroed before first use. slot >= M * N and even. Every rank
+ * must issue the same sequence of calls on one stream (a call's words alternate
+ * between two buffer halves by the call count kept in ctl); calls on a buffer
+ * must not overlap. Requirements as w4a16_gemm plus M <= 32, N % 8 == 0,
  * 16-byte-aligned inputs, 2 <= world <= 8. The workspace is w4a16_gemm's.
  */
 int w4a16_gemm_allreduce(const void* x, const int32_t* qweight, const void* scales,

@@ -91,24 +91,38 @@ struct Params {
   int num_stages;         // ring depth
   // Fused all-reduce (ar_world > 1): this rank's y is the sum over ranks of every
   // rank's partial GEMM (a row-parallel layer). Each rank owns one peer-to-peer
-  // buffer (layout below); ar_peers[q] is rank q's buffer as mapped on this GPU.
+  // buffer (layout below); ar_peer[q] is rank q's buffer as mapped on this GPU.
   int ar_world, ar_rank;
-  const unsigned long long* ar_peers;   // device array [ar_world]
-  int* ar_ctl;                          // this rank's control words: [0] epoch, [1] CTAs finished
-  long long ar_slot;                    // fp32 elements per rank slot (>= M * N)
+  int ar_tail;                          // CTAs that finish the call: the last ar_tail to arrive
+  int* ar_ctl;                          // this rank's control words: [0] epoch, [1] CTAs arrived
+  long long ar_slot;                    // elements per rank slot (>= M * N)
+  unsigned long long ar_peer[8];        // [ar_world] buffer addresses (kernel parameters)
 };
 
 // Peer-to-peer all-reduce buffer (one per rank): two halves, selected by the
-// epoch's parity, each with a flag per rank and a data slot per rank.
-//   [flags: 2 x AR_MAX_RANKS u32][pad to AR_DATA_OFF][data: 2 x world x slot fp32]
-// A rank writes its partial into its own slot of every rank's buffer, then the
-// epoch + 1 into its own flag of every rank's buffer. A rank can only be one
-// epoch ahead of another (it needs everyone's flag of the previous epoch before
-// its next launch), so the half it writes is never the one a peer still reads.
+// epoch's parity, each holding one slot per rank of 64-bit words
+//   word = (tag << 32) | fp32 bits,  tag = epoch + 1,   [2][world][slot]
+// The CTA that finalises output element e writes its word into slot `rank` of
+// every rank's buffer (one single-copy-atomic 64-bit store each, so the tag
+// vouches for the value beside it: no fence, no separate flag). A rank reads its
+// own buffer until every slot's word for its elements carries this epoch's tag.
+// A rank can only be one epoch ahead of another (it needs every rank's words of
+// the previous epoch to finish it), so the half it writes is never one a peer
+// still reads.
 constexpr int AR_MAX_RANKS = 8;
-constexpr long long AR_DATA_OFF = 256;   // bytes
 __host__ __device__ constexpr long long ar_buffer_bytes(int world, long long slot) {
-  return AR_DATA_OFF + 2ll * world * slot * 4;
+  return 2ll * world * slot * 8;
+}
+// Output elements each finishing thread takes (sets how many CTAs finish).
+constexpr int AR_ELEMS_PER_THREAD = 4;
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // c (+)= a * b on the tensor core, m16n8k16, fp16 in, fp32 accumulate.
@@ -156,11 +170,29 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
 }
 
-__device__ __forceinline__ void emit(const Params& p, int t, int n, float v, long long ar_off) {
-  if (p.ar_world > 1) {
-    // the unrounded partial into this rank's slot of its own buffer; the last CTA
-    // pushes the whole slot to the peers
-    reinterpret_cast<float*>(p.ar_peers[p.ar_rank])[ar_off + static_cast<long long>(t) * p.N + n] = v;
+__device__ __forceinline__ unsigned long long ld_shared_u64_volatile(uint32_t addr) {
+  unsigned long long v;
+  asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// peer_s: shared-memory copy of ar_peer, read at each store (volatile, so the
+// eight addresses are not hoisted into registers across the epilogue loops).
+template <bool AR>
+__device__ __forceinline__ void emit(const Params& p, int t, int n, float v, int ar_epoch,
+                                     uint32_t peer_s) {
+  if (AR) {
+    // the unrounded partial, tagged, into this rank's slot of every rank's buffer
+    // (the peers' first: they are the longer way)
+    const uint32_t tag = static_cast<uint32_t>(ar_epoch) + 1u;
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    const long long slot0 = (static_cast<long long>(ar_epoch & 1) * p.ar_world + p.ar_rank) * p.ar_slot;
+    const long long e8 = (slot0 + static_cast<long long>(t) * p.N + n) * 8;
+#pragma unroll
+    for (int q = 0; q < AR_MAX_RANKS; ++q)
+      if (q < p.ar_world && q != p.ar_rank)
+        st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(ld_shared_u64_volatile(peer_s + 8 * q) + e8), w);
+    st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(ld_shared_u64_volatile(peer_s + 8 * p.ar_rank) + e8), w);
     return;
   }
   const long long o = static_cast<long long>(t) * p.ldy + n;
@@ -173,7 +205,9 @@ __device__ __forceinline__ void emit(const Params& p, int t, int n, float v, lon
   static_cast<__half*>(p.y)[o] = h;
 }
 
-template <int MT>
+// AR: fused all-reduce (w4a16_gemm_allreduce); a separate instantiation so the
+// plain GEMM's register allocation is not shaped by it.
+template <int MT, bool AR>
 __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     decode_gemv_tma_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_s,
@@ -196,7 +230,8 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
   uint64_t* empty = full + nst;
   uint64_t* piece_ready = empty + nst;   // consumers -> publisher: first-strip piece parked
   uint64_t* published = piece_ready + 1; // publisher -> consumers: its arrival was counted
-  int* flag = reinterpret_cast<int*>(published + 1);
+  int* flag = reinterpret_cast<int*>(published + 1);                      // 16 ints
+  unsigned long long* ar_peer_smem = reinterpret_cast<unsigned long long*>(flag + 16);   // AR: [8]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -305,12 +340,9 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
 
   // Fused all-reduce: this launch's epoch (the previous launch on this stream has
   // completed, so its epoch advance is visible) and this rank's slot in the half.
-  int ar_epoch = 0;
-  long long ar_off = 0;
-  if (p.ar_world > 1) {
-    ar_epoch = *reinterpret_cast<volatile int*>(p.ar_ctl);
-    ar_off = AR_DATA_OFF / 4 + (static_cast<long long>(ar_epoch & 1) * p.ar_world + p.ar_rank) * p.ar_slot;
-  }
+  const int ar_epoch = AR ? *reinterpret_cast<volatile int*>(p.ar_ctl) : 0;
+  // the peers' addresses for emit (published to the consumers by their first barrier)
+  if (AR && threadIdx.x - 32 < AR_MAX_RANKS) ar_peer_smem[threadIdx.x - 32] = p.ar_peer[threadIdx.x - 32];
 
   // -------------------------------- consumers ---------------------------------
   const int cw = warp - 1;
@@ -461,7 +493,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
 #pragma unroll
           for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
           const int n = c * BN + cc;
-          if (n < p.N) emit(p, t, n, v, ar_off);
+          if (n < p.N) emit<AR>(p, t, n, v, ar_epoch, smem_u32(ar_peer_smem));
         }
       } else if (u != u1 - 1) {
         // the first strip, split and not the final segment: park its piece (slot 0)
@@ -528,7 +560,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
         for (int i = 0; i < MAXP; ++i) v += part[i];
       }
       const int n = cs * BN + cc;
-      if (n < p.N) emit(p, t, n, v, ar_off);
+      if (n < p.N) emit<AR>(p, t, n, v, ar_epoch, smem_u32(ar_peer_smem));
     }
   };
 
@@ -589,73 +621,67 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     }
   }
 
-  if (p.ar_world > 1) {
-    // ---------- fused all-reduce: the last CTA of this rank finishes the call ----------
+  if (AR) {
+    // ---------- fused all-reduce: the last ar_tail CTAs to arrive finish the call ----------
+    // Every element's word reaches every rank's buffer from the CTA that finalised
+    // it, so finishing needs no fence: a finishing CTA reads its share of the
+    // elements in every rank's slot until each word carries this epoch's tag (the
+    // words of this rank included), sums them in rank order and writes y. Only
+    // CTAs that have finished their own units wait, and they wait only on other
+    // CTAs' units, so the call completes whether or not the grid is co-resident.
     consumer_sync<NCW>();
     if (ctid == 0) {
-      __threadfence();   // this CTA's partials before its count
-      flag[3] = atomicAdd(p.ar_ctl + 1, 1) == static_cast<int>(gridDim.x) - 1 ? 1 : 0;
+      const int r = atomicAdd(p.ar_ctl + 1, 1);
+      const int grid = static_cast<int>(gridDim.x);
+      flag[3] = r - (grid - p.ar_tail);   // share index, negative: not finishing
+      if (r == grid - 1) {
+        // every CTA has read the epoch and arrived: advance both for the next launch
+        p.ar_ctl[1] = 0;
+        p.ar_ctl[0] = ar_epoch + 1;
+      }
     }
     consumer_sync<NCW>();
-    if (flag[3]) {
-      __threadfence();   // every CTA's partials (counted above) are visible to this CTA
-      const int half = ar_epoch & 1;
-      const unsigned tag = static_cast<unsigned>(ar_epoch) + 1u;
-      const int total = M * p.N;   // N % 8 == 0: whole float4s
-      const float* mine = reinterpret_cast<const float*>(p.ar_peers[p.ar_rank]) + ar_off;
-      // push this rank's slot into every peer's buffer (vector stores over NVLink)
-      for (int q = 0; q < p.ar_world; ++q) {
-        if (q == p.ar_rank) continue;
-        float* dst = reinterpret_cast<float*>(p.ar_peers[q]) + ar_off;
-        for (int i = ctid * 4; i < total; i += NCW * 32 * 4)
-          *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(mine + i));
-      }
-      consumer_sync<NCW>();
-      if (ctid == 0) {
-        __threadfence_system();   // the pushed slots before the flags
-        p.ar_ctl[1] = 0;   // the next launch counts from zero
-        for (int q = 0; q < p.ar_world; ++q) {
-          unsigned* f = reinterpret_cast<unsigned*>(p.ar_peers[q]) + half * AR_MAX_RANKS + p.ar_rank;
-          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(tag) : "memory");
-        }
-      }
-      // every rank's flag in this rank's own buffer (bounded wait)
-      if (ctid < p.ar_world) {
-        const unsigned* f = reinterpret_cast<const unsigned*>(p.ar_peers[p.ar_rank]) + half * AR_MAX_RANKS + ctid;
-        const uint64_t t0 = global_timer_ns();
-        for (uint32_t i = 0;; ++i) {
-          unsigned v;
-          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-          if (v == tag) break;
-          if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitBudgetNs) {
-            flag_error(kErrWaitTimeout);
-            break;
-          }
-        }
-      }
-      consumer_sync<NCW>();
-      // y = fp16(sum of the ranks' partials, in rank order) [+ bias, rounded again]
-      const float* own = reinterpret_cast<const float*>(p.ar_peers[p.ar_rank]) + AR_DATA_OFF / 4 +
-                         static_cast<long long>(half) * p.ar_world * p.ar_slot;
-      for (int i = ctid * 4; i < total; i += NCW * 32 * 4) {
-        float4 v = __ldcg(reinterpret_cast<const float4*>(own + i));
-        for (int q = 1; q < p.ar_world; ++q) {
-          const float4 w = __ldcg(reinterpret_cast<const float4*>(own + q * p.ar_slot + i));
-          v.x += w.x;
-          v.y += w.y;
-          v.z += w.z;
-          v.w += w.w;
-        }
-        const float e[4] = {v.x, v.y, v.z, v.w};
+    const int share = flag[3];
+    if (share >= 0) {
+      const long long total = static_cast<long long>(M) * p.N;
+      const long long per = (total + p.ar_tail - 1) / p.ar_tail;
+      const long long lo = share * per;
+      const long long hi = lo + per < total ? lo + per : total;
+      const unsigned long long* half_base =
+          reinterpret_cast<const unsigned long long*>(p.ar_peer[p.ar_rank]) +
+          static_cast<long long>(ar_epoch & 1) * p.ar_world * p.ar_slot;
+      const uint32_t ar_tag = static_cast<uint32_t>(ar_epoch) + 1u;
+      bool waiting = true;   // false once this thread's wait budget ran out
+      for (long long e = lo + ctid; e < hi; e += NCW * 32) {
+        unsigned long long w[AR_MAX_RANKS];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int idx = i + j, t = idx / p.N, n = idx - t * p.N;
-          __half h = __float2half_rn(e[j]);
-          if (p.bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(p.bias[n]));
-          static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + n] = h;
+        for (int q = 0; q < AR_MAX_RANKS; ++q)
+          if (q < p.ar_world) w[q] = ld_volatile_u64(half_base + q * p.ar_slot + e);
+        float a = 0.0f;
+#pragma unroll
+        for (int q = 0; q < AR_MAX_RANKS; ++q) {
+          if (q >= p.ar_world) break;
+          uint64_t t0 = 0;
+          for (uint32_t it = 0; waiting && static_cast<uint32_t>(w[q] >> 32) != ar_tag; ++it) {
+            if (it == 0) {
+              t0 = global_timer_ns();
+            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+              flag_error(kErrWaitTimeout);
+              waiting = false;
+              break;
+            }
+            __nanosleep(32);
+            w[q] = ld_volatile_u64(half_base + q * p.ar_slot + e);
+          }
+          const float v = __uint_as_float(static_cast<uint32_t>(w[q]));
+          a = q == 0 ? v : a + v;   // rank order
         }
+        // y = fp16(sum) [+ bias, rounded again]
+        const int t = static_cast<int>(e / p.N), n = static_cast<int>(e - static_cast<long long>(t) * p.N);
+        __half h = __float2half_rn(a);
+        if (p.bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(p.bias[n]));
+        static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + n] = h;
       }
-      if (ctid == 0) p.ar_ctl[0] = ar_epoch + 1;   // the next launch's epoch
     }
   }
 }

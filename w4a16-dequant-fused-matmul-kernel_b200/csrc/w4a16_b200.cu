@@ -74,10 +74,14 @@ int current_device_state(DeviceState** out) {
              cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) ==
                  cudaSuccess;
     };
-    if (!set_decode(decode::decode_gemv_tma_kernel<1>) ||
-        !set_decode(decode::decode_gemv_tma_kernel<2>) ||
-        !set_decode(decode::decode_gemv_tma_kernel<3>) ||
-        !set_decode(decode::decode_gemv_tma_kernel<4>)) {
+    if (!set_decode(decode::decode_gemv_tma_kernel<1, false>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<2, false>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<3, false>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<4, false>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<1, true>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<2, true>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<3, true>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<4, true>)) {
       cudaGetLastError();
       return W4A16_ERR_LAUNCH;
     }
@@ -194,7 +198,7 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
   d.nst = nst;
   d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) +
-           (2 * nst + 2) * sizeof(uint64_t) + 64;
+           (2 * nst + 2) * sizeof(uint64_t) + 64 + 64;
   long long grid = static_cast<long long>(dev.num_sms) * decode::ctas_per_sm(d.MT);
   if (grid > d.units) grid = d.units;
   d.grid = static_cast<int>(grid);
@@ -207,7 +211,7 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
 // Fused all-reduce arguments of the decode kernel (world 0: off).
 struct ArArgs {
   int world = 0, rank = 0;
-  const unsigned long long* peers = nullptr;
+  const unsigned long long* peers = nullptr;   // host array [world]
   int* ctl = nullptr;
   long long slot = 0;
 };
@@ -250,9 +254,17 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.num_stages = d.nst;
   p.ar_world = ar.world;
   p.ar_rank = ar.rank;
-  p.ar_peers = ar.peers;
   p.ar_ctl = ar.ctl;
   p.ar_slot = ar.slot;
+  p.ar_tail = 0;
+  for (int q = 0; q < decode::AR_MAX_RANKS; ++q) p.ar_peer[q] = q < ar.world ? ar.peers[q] : 0ull;
+  if (ar.world > 1) {
+    // enough finishing CTAs that each thread sums AR_ELEMS_PER_THREAD elements
+    const long long per_cta = static_cast<long long>(decode::ncw_for(d.MT)) * 32 * decode::AR_ELEMS_PER_THREAD;
+    const long long elems = static_cast<long long>(M) * N;
+    const long long tail = (elems + per_cta - 1) / per_cta;
+    p.ar_tail = static_cast<int>(tail < 1 ? 1 : (tail > d.grid ? d.grid : tail));
+  }
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(d.grid), 1, 1);
@@ -265,11 +277,16 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e;
-  switch (d.MT) {
-    case 1: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1>, tw, ts, tz, tx, p); break;
-    case 2: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2>, tw, ts, tz, tx, p); break;
-    case 3: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<3>, tw, ts, tz, tx, p); break;
-    default: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<4>, tw, ts, tz, tx, p); break;
+  const bool fused = ar.world > 1;
+  switch (d.MT * 2 + (fused ? 1 : 0)) {
+    case 2: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1, false>, tw, ts, tz, tx, p); break;
+    case 3: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1, true>, tw, ts, tz, tx, p); break;
+    case 4: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2, false>, tw, ts, tz, tx, p); break;
+    case 5: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2, true>, tw, ts, tz, tx, p); break;
+    case 6: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<3, false>, tw, ts, tz, tx, p); break;
+    case 7: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<3, true>, tw, ts, tz, tx, p); break;
+    case 8: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<4, false>, tw, ts, tz, tx, p); break;
+    default: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<4, true>, tw, ts, tz, tx, p); break;
   }
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -694,6 +711,8 @@ extern "C" int w4a16_gemm_allreduce(const void* x, const int32_t* qweight, const
   if (ldy < N || M > 32 || N % 8 != 0) return W4A16_ERR_INVALID;
   if (world < 2 || world > decode::AR_MAX_RANKS || rank < 0 || rank >= world) return W4A16_ERR_INVALID;
   if (peers == nullptr || ctl == nullptr || slot < M * N) return W4A16_ERR_INVALID;
+  for (int q = 0; q < world; ++q)
+    if (peers[q] == 0ull || (peers[q] & 15ull) != 0ull) return W4A16_ERR_ALIGNMENT;
   if (M == 0 || N == 0) return W4A16_OK;
   if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || y == nullptr)
     return W4A16_ERR_INVALID;

@@ -2,12 +2,13 @@
 
 ``PeerAllReduce`` owns, on every rank of a process group, one CUDA IPC buffer
 mapped on every other rank (plain peer memory over NVLink / NVSwitch; no
-multicast object), a device array of those mappings and two control words. A
+multicast object), the list of those mappings and two device control words. A
 call runs ``w4a16_gemm_allreduce``: one kernel per rank computes its partial
-GEMM, writes it into every rank's buffer and, in its last CTA, waits for the
-other ranks' partials and sums them in rank order -- the GEMM and the
-all-reduce of a row-parallel layer in one launch, with the same result as an
-fp32 all-reduce followed by one fp16 rounding.
+GEMM and writes each finished fp32 element, tagged with the call's epoch, into
+every rank's buffer; its last CTAs wait for every rank's tagged elements of
+their share and sum them in rank order -- the GEMM and the all-reduce of a
+row-parallel layer in one launch, with the same result as an fp32 all-reduce
+followed by one fp16 rounding.
 
 Creating a channel is collective (every rank of the group, same order, same
 arguments); so is every call. Calls on one channel must be issued on one
@@ -43,7 +44,7 @@ class PeerAllReduce:
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.n = n
         self.max_tokens = max_tokens
-        self.slot = max_tokens * n
+        self.slot = (max_tokens * n + 1) // 2 * 2   # even: the kernel reads word pairs
         lib = _lib.lib()
         nbytes = ctypes.c_int64(0)
         _lib.check(lib.w4a16_p2p_buffer_bytes(self.world, self.slot, ctypes.byref(nbytes)),
@@ -66,7 +67,7 @@ class PeerAllReduce:
                 _lib.check(lib.w4a16_p2p_open(hb, ctypes.byref(p)), "w4a16_p2p_open")
                 ptrs.append(p.value)
                 self._opened.append(p.value)
-        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.peers = (ctypes.c_ulonglong * self.world)(*ptrs)   # host array, copied into each launch
         self.ctl = torch.zeros(4, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)   # every buffer is mapped and zero before the first call
@@ -86,7 +87,7 @@ class PeerAllReduce:
         st = _lib.lib().w4a16_gemm_allreduce(
             x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), _lib.ptr(bias),
             y.data_ptr(), M, N, K, group_size, N, _lib.ptr(ws), 0 if ws is None else ws.numel(),
-            self.peers.data_ptr(), self.world, self.rank, self.ctl.data_ptr(), self.slot, stream)
+            self.peers, self.world, self.rank, self.ctl.data_ptr(), self.slot, stream)
         _lib.check(st, "w4a16_gemm_allreduce")
         return y
 
