@@ -64,13 +64,13 @@ const char* w4a16_strerror(int status);
  * launches over 32-row slices of x).
  *
  * workspace: device scratch of at least w4a16_gemm_workspace_size() bytes,
- * 256-byte aligned, ZEROED before its first use. The decode kernel keeps
- * per-strip arrival counters and partial sums there and leaves the counters
- * zero again when it completes, so one zeroed buffer serves every later call
- * on the same stream; launches that may run concurrently need separate
- * workspaces. (A launch abandoned on W4A16_ERR_TIMEOUT can leave counters
- * set: zero the buffer again before reusing it.) May be NULL when the size
- * query returned 0.
+ * 256-byte aligned, ZEROED before its first use. The decode kernel passes the
+ * partial sums of column strips shared by two or more CTAs through it (tagged
+ * 64-bit words) and leaves it zero again when it completes, so one zeroed
+ * buffer serves every later call on the same stream, whatever the shape;
+ * launches that may run concurrently need separate workspaces. (A launch
+ * abandoned on W4A16_ERR_TIMEOUT can leave words set: zero the buffer again
+ * before reusing it.) May be NULL when the size query returned 0.
  */
 int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales,
                const void* zeros, const void* bias, void* y,
@@ -154,21 +154,20 @@ int w4a16_check_device_errors(void* stream, uint32_t* flags_out);
  * For callers that cannot allocate device memory at call time: a C or FFI
  * host with no device allocator of its own, an engine whose memory planner
  * has already handed out all device memory, or a plugin interface whose
- * launch call passes no scratch buffer. The decode kernel's scratch (strip
- * arrival counters and partial sums) lives instead in one static device
+ * launch call passes no scratch buffer. The decode kernel's scratch (the
+ * partial sums of shared column strips) lives instead in one static device
  * array inside this library, W4A16_NOALLOC_SCRATCH_BYTES per device, whose
  * address the library looks up once per device. Shapes whose decode launch
  * would need more than that return W4A16_ERR_SCRATCH_LIMIT (on a 148-SM B200
- * every shape fits: the need is 64 KiB + SMs * M-tiles * 64 KiB, at most
- * about 4.7 MiB); prefill shapes need no scratch.
+ * every shape fits: the need is CTAs * M-tiles * 8 KiB, at most 148 * 4 *
+ * 8 KiB = 4.6 MiB); prefill shapes need no scratch.
  *
  * The first call on each device does the set-up: it looks the array up,
- * zeroes its counter region on `stream` and synchronises that stream. Make
- * that first call before any stream capture; a first call made while
- * `stream` is capturing returns W4A16_ERR_INVALID. The counters must be zero
- * whenever a decode launch starts: set-up zeroes them and every completed
- * launch leaves them zero, but a launch abandoned on W4A16_ERR_TIMEOUT may
- * not. There is ONE scratch array per device, so calls whose kernels can run
+ * zeroes it on `stream` and synchronises that stream. Make that first call
+ * before any stream capture; a first call made while `stream` is capturing
+ * returns W4A16_ERR_INVALID. The array must be zero whenever a decode launch
+ * starts: set-up zeroes it and every completed launch leaves it zero, but a
+ * launch abandoned on W4A16_ERR_TIMEOUT may not. There is ONE scratch array per device, so calls whose kernels can run
  * at the same time (different streams, threads or processes sharing a
  * context, parallel graph branches) race on it and give wrong results: keep
  * every call on one device ordered, or use w4a16_gemm with a workspace per

@@ -31,14 +31,17 @@
 //    product unchanged).
 //  * A strip covered by one CTA is reduced in shared memory and written
 //    directly. Each CTA shares at most two strips (its first and last) with
-//    neighbours. Its first strip ends early in its range: the consumers park
-//    that piece in the caller's workspace and an idle lane of the producer warp
-//    fences and counts the arrival, off the consumers' path. At the end, the
-//    CTA reads its last strip's counter: when every other piece has arrived
-//    (the usual case) it is the last arriver without publishing its own piece;
-//    otherwise it publishes and counts like the others. The last arriver sums
-//    all pieces in CTA order -- deterministic -- writes y and resets the
-//    counter, leaving the workspace clean for the next launch.
+//    neighbours. A shared strip belongs to the CTA that holds its last K stage
+//    (its "owner"); every earlier CTA of the strip ends its range inside it and
+//    publishes its fp32 piece as 64-bit words (1 << 32 | bits) in its own
+//    workspace slot: a 64-bit store is single-copy atomic, so the tag vouches
+//    for the value and no fence or counter is needed. The owner parks its own
+//    piece in shared memory when the strip ends mid-range, and at the end of its
+//    range reads the other pieces until their tags are set, sums all pieces in
+//    CTA order -- deterministic -- writes y and clears the tags, leaving the
+//    workspace zeroed for the next launch. Only finished CTAs wait, and only on
+//    other CTAs' units, so the launch completes even if its CTAs are not all
+//    resident at once.
 #pragma once
 
 #include "common.cuh"
@@ -53,11 +56,10 @@ constexpr int SZ_ROWS = 8;          // scale/zero rows per stage (G >= 64 => at 
 constexpr int W_BYTES = ROWS * BN * 4;        // 32768
 constexpr int SZ_BYTES = SZ_ROWS * BN * 2;    // 2048 (each of scales, zeros)
 constexpr int XBOX = 256;                     // K width of one x box (TMA box sides <= 256)
-// Workspace layout: strip arrival counters in a fixed region at offset 0 (so
-// that launches of any shape never write partial sums over another shape's
-// counters), then the partial sums.
+// Workspace: one slot of tagged piece words per CTA, [gridDim.x][MT*8][BN]
+// 64-bit words, all zero between launches.
 constexpr int MAX_STRIPS = 16384;             // N <= 2,097,152 on the decode path
-constexpr size_t COUNTER_BYTES = MAX_STRIPS * sizeof(unsigned);
+constexpr unsigned long long PIECE_TAG = 1ull << 32;
 
 // Consumer warps: 4 column quarters x 2 K halves of 256 = 8 warps for every
 // token count. (16 warps with K quarters were measured 5% slower at M = 1 on
@@ -72,6 +74,8 @@ __host__ __device__ constexpr int ctas_per_sm(int MT) { return MT == 1 ? 2 : 1; 
 __host__ __device__ constexpr int x_bytes(int M) { return KSTAGE * 2 * M; }
 __host__ __device__ constexpr int stage_bytes(int M) { return W_BYTES + 2 * SZ_BYTES + x_bytes(M); }
 __host__ __device__ constexpr int red_bytes(int MT) { return (ncw_for(MT) / 4) * (MT * 8) * BN * 4; }
+// the owner's parked piece of its first strip: [MT*8][BN] fp32
+__host__ __device__ constexpr int park_bytes(int MT) { return (MT * 8) * BN * 4; }
 // TMA destinations within a stage (W, S, Z, x box 0, x box 1) are 128-byte aligned.
 static_assert(W_BYTES % 128 == 0 && SZ_BYTES % 128 == 0 && (XBOX * 2) % 128 == 0 &&
                   stage_bytes(1) % 1024 == 0,
@@ -81,8 +85,7 @@ struct Params {
   const __half* bias;
   void* y;                // fp16, or fp32 when y_f32 (unrounded partial sums, no bias)
   int y_f32;
-  float* partials;        // [gridDim.x][2][MT*8][BN] fp32 partial sums of shared strips
-  unsigned* counters;     // [strips] arrival counters, zero between launches
+  unsigned long long* pieces;   // [gridDim.x][MT*8][BN] tagged piece words, zero between launches
   int M, N, K, G;
   int g_shift;            // log2(G) when G is a power of two, else -1
   long long ldy;
@@ -116,6 +119,14 @@ __host__ __device__ constexpr long long ar_buffer_bytes(int world, long long slo
 // Output elements each finishing thread takes (sets how many CTAs finish).
 constexpr int AR_ELEMS_PER_THREAD = 4;
 
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -226,11 +237,10 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
   const int nst = p.num_stages;
   const int sbytes = stage_bytes(M);
   float* red = reinterpret_cast<float*>(smem + nst * sbytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * sbytes + red_bytes(MT));
+  float* park = reinterpret_cast<float*>(smem + nst * sbytes + red_bytes(MT));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * sbytes + red_bytes(MT) + park_bytes(MT));
   uint64_t* empty = full + nst;
-  uint64_t* piece_ready = empty + nst;   // consumers -> publisher: first-strip piece parked
-  uint64_t* published = piece_ready + 1; // publisher -> consumers: its arrival was counted
-  int* flag = reinterpret_cast<int*>(published + 1);                      // 16 ints
+  int* flag = reinterpret_cast<int*>(empty + nst);                       // 16 ints
   unsigned long long* ar_peer_smem = reinterpret_cast<unsigned long long*>(flag + 16);   // AR: [8]
 
   const int warp = threadIdx.x >> 5;
@@ -244,13 +254,13 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
   const int k_first = static_cast<int>(u0 - static_cast<long long>(c_first) * KS);
   const int c_last = static_cast<int>((u1 - 1) / KS);
   const int k_last = static_cast<int>((u1 - 1) - static_cast<long long>(c_last) * KS);
-  // A strip is "split" when other CTAs hold part of its K range. This CTA's first
-  // strip may be split (then it is its neighbours' last strip), and so may its
-  // last strip; when both are the same strip there is a single split segment.
-  const bool first_split = !(k_first == 0 && (c_last > c_first || k_last == KS - 1));
-  const bool last_split = c_last > c_first && k_last != KS - 1;
-  const bool first_early = first_split && c_last > c_first;        // published mid-stream
-  const bool final_split = last_split || (first_split && c_last == c_first);
+  // A strip is "split" when other CTAs hold part of its K range. This CTA owns
+  // its first strip when that strip began in an earlier CTA and ends in this
+  // range; it publishes its last segment when its last strip continues in a
+  // later CTA. (Both can hold; when the range lies inside one strip that began
+  // earlier and continues later, it only publishes.)
+  const bool owns_first = k_first != 0 && (c_last > c_first || k_last == KS - 1);
+  const bool publishes = k_last != KS - 1;
 
   if (threadIdx.x == 0) {
     pdl_launch_dependents();
@@ -258,8 +268,6 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NCW);
     }
-    mbar_init(piece_ready, NCW);
-    mbar_init(published, 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -317,22 +325,6 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
         --s;
         mbar_wait(&full[s], ph);
       }
-    }
-    if (lane == 1 && first_early) {
-      // Publisher for the first (split) strip, off the consumers' path: once they
-      // have parked its piece, make it visible device-wide and count the arrival.
-      // (Release chain: consumers' stores -> mbarrier arrive -> this wait -> fence.)
-      pdl_wait();
-      int last = 0;
-      if (mbar_wait(piece_ready, 0)) {
-        __threadfence();
-        const long long lo = static_cast<long long>(c_first) * KS, hi = lo + KS - 1;
-        const long long pf = ((lo + 1) * P + U - 1) / U - 1;
-        const long long pl = ((hi + 1) * P + U - 1) / U - 1;
-        last = atomicAdd(&p.counters[c_first], 1u) == static_cast<unsigned>(pl - pf) ? 1 : 0;
-      }
-      flag[2] = last;
-      mbar_arrive(published);
     }
     return;   // takes no part in the consumers' barriers below
   }
@@ -496,128 +488,79 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           if (n < p.N) emit<AR>(p, t, n, v, ar_epoch, smem_u32(ar_peer_smem));
         }
       } else if (u != u1 - 1) {
-        // the first strip, split and not the final segment: park its piece (slot 0)
-        // and hand it to the publisher lane
-        float* dst = p.partials + static_cast<long long>(blockIdx.x) * 2 * (MT * 8) * BN;
+        // the first strip, which this CTA owns, ends here mid-range: park its piece
         for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
           const int t = idx / BN, cc = idx % BN;
           float v = 0.0f;
 #pragma unroll
           for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
-          dst[t * BN + cc] = v;
+          park[t * BN + cc] = v;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(piece_ready);
       }
-      // (the final split segment keeps its piece in red[] for the fix-up below)
+      // (a final segment that is not a whole strip keeps its piece in red[] for below)
       if (u != u1 - 1) consumer_sync<NCW>();   // red[] is reused by the next segment
     }
     if (++k == KS) { k = 0; ++c; }
   }
 
-  // ---------------- shared strips: the last CTA to arrive sums and emits ----------------
-  // Pieces are summed in CTA order whoever sums them, so y is deterministic. The
-  // strip's first CTA holds its piece in slot 1 (the strip is its last one) unless
-  // the strip is also its first; every later CTA holds it in slot 0.
-  auto piece_range = [&](int cs, int& pf, int& pl, int& pf_slot) {
-    const long long lo = static_cast<long long>(cs) * KS, hi = lo + KS - 1;
-    pf = static_cast<int>(((lo + 1) * P + U - 1) / U - 1);
-    pl = static_cast<int>(((hi + 1) * P + U - 1) / U - 1);
-    pf_slot = (unit_begin(pf, U, P) / KS == cs) ? 0 : 1;
+  // ---------------- shared strips: publish the final piece, finish the owned strip ----------------
+  const float* own_red = red;   // this CTA's piece of its final segment: sum over the K parts
+  auto own_final = [&](int t, int cc) {
+    float v = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KQ; ++j) v += own_red[(j * MT * 8 + t) * BN + cc];
+    return v;
   };
-  // y[:, strip cs] = sum of the pieces pf..pl; this CTA's own piece comes from red[]
-  // when own_in_red (it was never written out), else from the workspace.
-  auto sum_strip = [&](int cs, bool own_in_red) {
-    int pf, pl, pf_slot;
-    piece_range(cs, pf, pl, pf_slot);
+  if (publishes) {
+    // the last strip continues in the next CTA: this segment is a piece for its owner
+    unsigned long long* dst = p.pieces + static_cast<long long>(blockIdx.x) * (MT * 8) * BN;
+    for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
+      const int t = idx / BN, cc = idx % BN;
+      st_relaxed_gpu_u64(dst + t * BN + cc, PIECE_TAG | __float_as_uint(own_final(t, cc)));
+    }
+  }
+  if (owns_first) {
+    // y[:, strip c_first] = the pieces of CTAs pf .. this one, summed in CTA order
+    const int cs = c_first;
+    const long long lo = static_cast<long long>(cs) * KS;
+    const int pf = static_cast<int>(((lo + 1) * P + U - 1) / U - 1);
     const int me = static_cast<int>(blockIdx.x);
+    const bool own_parked = c_last > c_first;   // else the strip is the final segment, in red[]
+    bool waiting = true;                        // false once this thread's wait budget ran out
     for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
       const int t = idx / BN, cc = idx % BN;
       const long long off = static_cast<long long>(t) * BN + cc;
-      float own = 0.0f;
-      if (own_in_red) {
-#pragma unroll
-        for (int j = 0; j < KQ; ++j) own += red[(j * MT * 8 + t) * BN + cc];
-      }
       constexpr int MAXP = 8;   // pieces fetched before summing (more are summed in a loop)
       float v = 0.0f;
-      for (int base = pf; base <= pl; base += MAXP) {
-        float part[MAXP];
+      for (int base = pf; base < me; base += MAXP) {
+        unsigned long long w[MAXP];
+#pragma unroll
+        for (int i = 0; i < MAXP; ++i)
+          w[i] = base + i < me ? ld_relaxed_gpu_u64(p.pieces + static_cast<long long>(base + i) * (MT * 8) * BN + off)
+                               : PIECE_TAG;
 #pragma unroll
         for (int i = 0; i < MAXP; ++i) {
-          const int pp = base + i;
-          part[i] = 0.0f;
-          if (pp <= pl) {
-            if (pp == me && own_in_red) {
-              part[i] = own;
-            } else {
-              const int slot = (pp == pf) ? pf_slot : 0;
-              part[i] = __ldcg(p.partials + (static_cast<long long>(pp) * 2 + slot) * (MT * 8) * BN + off);
+          if (base + i >= me) break;
+          unsigned long long* src = p.pieces + static_cast<long long>(base + i) * (MT * 8) * BN + off;
+          uint64_t t0 = 0;
+          for (uint32_t it = 0; waiting && (w[i] >> 32) != 1ull; ++it) {
+            if (it == 0) {
+              t0 = global_timer_ns();
+            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+              flag_error(kErrWaitTimeout);
+              waiting = false;
+              break;
             }
+            __nanosleep(32);
+            w[i] = ld_relaxed_gpu_u64(src);
           }
+          v += __uint_as_float(static_cast<uint32_t>(w[i]));
+          st_relaxed_gpu_u64(src, 0ull);   // consumed: the slot is zero for the next launch
         }
-#pragma unroll
-        for (int i = 0; i < MAXP; ++i) v += part[i];
       }
+      v += own_parked ? park[t * BN + cc] : own_final(t, cc);
       const int n = cs * BN + cc;
       if (n < p.N) emit<AR>(p, t, n, v, ar_epoch, smem_u32(ar_peer_smem));
-    }
-  };
-
-  if (final_split) {
-    const int cs = c_last;
-    int pf, pl, pf_slot;
-    piece_range(cs, pf, pl, pf_slot);
-    // When this CTA starts a two-piece strip whose other CTA continues past it,
-    // that CTA published its piece early (its first strip), so usually it is
-    // already counted: then this CTA is last without writing its own piece or
-    // counting itself. (A strip with a middle CTA gets its pieces late; there
-    // the check would only add a round trip.)
-    const long long pl_end = unit_begin(pl + 1, U, P);   // one past the last unit of CTA pl
-    const bool early_partner = pf == static_cast<int>(blockIdx.x) && pl == pf + 1 &&
-                               (pl_end - 1) / KS > cs;
-    bool last = false;
-    if (early_partner) {
-      if (ctid == 0) {
-        unsigned cnt;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cnt) : "l"(p.counters + cs) : "memory");
-        flag[0] = cnt == 1u ? 1 : 0;
-      }
-      consumer_sync<NCW>();
-      last = flag[0] != 0;
-    }
-    if (!last) {
-      float* dst = p.partials + (static_cast<long long>(blockIdx.x) * 2 + (c_last == c_first ? 0 : 1)) *
-                                    (MT * 8) * BN;
-      for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
-        const int t = idx / BN, cc = idx % BN;
-        float v = 0.0f;
-#pragma unroll
-        for (int j = 0; j < KQ; ++j) v += red[(j * MT * 8 + t) * BN + cc];
-        dst[t * BN + cc] = v;
-      }
-      consumer_sync<NCW>();
-      if (ctid == 0) {
-        __threadfence();
-        flag[1] = atomicAdd(&p.counters[cs], 1u) == static_cast<unsigned>(pl - pf) ? 1 : 0;
-      }
-      consumer_sync<NCW>();
-      last = flag[1] != 0;
-      if (last) __threadfence();   // acquire side: the others' pieces are read below
-    }
-    if (last) {
-      if (ctid == 0) p.counters[cs] = 0u;   // last arrival: leave the workspace clean
-      sum_strip(cs, true);
-    }
-  }
-  if (first_early) {
-    // the publisher's verdict on the first strip
-    if (lane == 0) mbar_wait(published, 0);
-    __syncwarp();
-    if (flag[2]) {
-      __threadfence();
-      if (ctid == 0) p.counters[c_first] = 0u;
-      sum_strip(c_first, false);
     }
   }
 

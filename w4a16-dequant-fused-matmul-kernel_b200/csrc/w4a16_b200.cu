@@ -180,8 +180,8 @@ struct DecodePlan {
   int MT = 1, nst = 2, grid = 0, kstages = 0, chunks = 0;
   long long units = 0;
   size_t smem = 0;
-  size_t partial_bytes = 0, counter_bytes = 0;
-  size_t workspace() const { return counter_bytes + partial_bytes; }
+  size_t piece_bytes = 0;
+  size_t workspace() const { return piece_bytes; }
 };
 
 int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
@@ -194,16 +194,15 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   // Ring depth: ~190 KB of stages plus the reduction buffer per SM, split between the CTAs
   // that share an SM (>= 2, <= 8 stages per CTA).
   const int ring_budget = (decode::ctas_per_sm(d.MT) == 2 ? 108 : 190) * 1024;
-  int nst = (ring_budget - decode::red_bytes(d.MT)) / sbytes;
+  int nst = (ring_budget - decode::red_bytes(d.MT) - decode::park_bytes(d.MT)) / sbytes;
   nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
   d.nst = nst;
-  d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) +
-           (2 * nst + 2) * sizeof(uint64_t) + 64 + 64;
+  d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) + decode::park_bytes(d.MT) +
+           2 * nst * sizeof(uint64_t) + 64 + 64;
   long long grid = static_cast<long long>(dev.num_sms) * decode::ctas_per_sm(d.MT);
   if (grid > d.units) grid = d.units;
   d.grid = static_cast<int>(grid);
-  d.partial_bytes = static_cast<size_t>(d.grid) * 2 * (d.MT * 8) * decode::BN * sizeof(float);
-  d.counter_bytes = decode::COUNTER_BYTES;
+  d.piece_bytes = static_cast<size_t>(d.grid) * (d.MT * 8) * decode::BN * sizeof(unsigned long long);
   *out = d;
   return W4A16_OK;
 }
@@ -241,8 +240,7 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.bias = bias;
   p.y = y;
   p.y_f32 = y_f32;
-  p.counters = static_cast<unsigned*>(workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + d.counter_bytes);
+  p.pieces = static_cast<unsigned long long*>(workspace);
   p.M = M;
   p.N = N;
   p.K = K;
@@ -623,12 +621,11 @@ int w4a16_check_device_errors(void* stream, uint32_t* flags_out) {
 // For callers that cannot allocate device memory when they launch (a C/FFI
 // host without a device allocator, an engine whose planner owns all device
 // memory, a plugin call that passes no scratch): the decode kernel's scratch
-// is this static array instead of a caller workspace. Layout as a workspace:
-// strip counters (decode::COUNTER_BYTES, must be zero when a launch starts)
-// at offset 0, partial sums after them. One array per device, so launches
-// that overlap in time race on it; callers keep them ordered.
+// is this static array instead of a caller workspace, used exactly as one: the
+// tagged piece words of shared strips, which must be zero when a launch starts
+// (every launch leaves them zero). One array per device, so launches that
+// overlap in time race on it; callers keep them ordered.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[W4A16_NOALLOC_SCRATCH_BYTES];
-static_assert(decode::COUNTER_BYTES < W4A16_NOALLOC_SCRATCH_BYTES, "scratch holds the counters");
 
 namespace {
 struct NoallocScratch {
@@ -639,8 +636,8 @@ NoallocScratch g_noalloc[w4a16::kMaxDevices];
 std::mutex g_noalloc_mu;
 
 // Once per device, with that device current: the array's device address
-// (host code never passes the symbol itself to a kernel) and its counter
-// region zeroed on `stream`, which is then synchronised. Refused while
+// (host code never passes the symbol itself to a kernel) and the whole array
+// zeroed on `stream`, which is then synchronised. Refused while
 // `stream` is capturing, since neither step belongs in a graph.
 int noalloc_scratch(cudaStream_t stream, void** out) {
   int dev = 0;
@@ -663,7 +660,7 @@ int noalloc_scratch(cudaStream_t stream, void** out) {
       cudaGetLastError();
       return W4A16_ERR_LAUNCH;
     }
-    if (cudaMemsetAsync(ptr, 0, decode::COUNTER_BYTES, stream) != cudaSuccess ||
+    if (cudaMemsetAsync(ptr, 0, W4A16_NOALLOC_SCRATCH_BYTES, stream) != cudaSuccess ||
         cudaStreamSynchronize(stream) != cudaSuccess) {
       cudaGetLastError();
       return W4A16_ERR_LAUNCH;

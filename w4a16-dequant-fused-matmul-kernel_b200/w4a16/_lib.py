@@ -123,7 +123,7 @@ def check_device_errors(device: torch.device | int | None = None) -> int:
 
 # ---------------------------------------------------------------------------
 # GEMM workspace: one zeroed buffer per (device, stream), grown on demand. The
-# decode kernel leaves its counters zero after every launch, so the buffer is
+# decode kernel leaves it zero after every launch, so the buffer is
 # reused without clearing. Superseded buffers are kept alive because a CUDA
 # graph captured earlier may still refer to them.
 # ---------------------------------------------------------------------------
