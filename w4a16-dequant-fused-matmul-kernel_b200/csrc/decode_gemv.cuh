@@ -344,15 +344,11 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
   const int q = lane >> 2;        // MMA group id: columns 4q..4q+3 of the quarter
   const int g = lane & 3;         // MMA thread-in-group: packed row within a quad
   const int ccol = cq * 32 + 4 * q;
-  // x rows this lane feeds to its MMA column q of each token tile (token tt*8 + q)
-  uint32_t xmask[MT];
+  // x rows this lane feeds to its MMA column q of each token tile (token tt*8 + q;
+  // token 0's row stands in for tokens that do not exist)
   int xoff[MT];
 #pragma unroll
-  for (int tt = 0; tt < MT; ++tt) {
-    const bool valid = tt * 8 + q < M;
-    xmask[tt] = valid ? 0xFFFFFFFFu : 0u;
-    xoff[tt] = valid ? (tt * 8 + q) * (XBOX * 2) : 0;
-  }
+  for (int tt = 0; tt < MT; ++tt) xoff[tt] = tt * 8 + q < M ? (tt * 8 + q) * (XBOX * 2) : 0;
 
   float acc[2][2][MT][4];         // [quad parity][column tile][token tile][fragment]
   int s = 0;
@@ -419,20 +415,10 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           uint4 xv[MT];
 #pragma unroll
           for (int tt = 0; tt < MT; ++tt) {
-            uint4 v;
-            if constexpr (MT <= 2) {
-              // branch-free: lanes whose token does not exist read token 0's row and mask
-              // it (a divergent branch per quad costs more than the load)
-              v = *reinterpret_cast<const uint4*>(xq + xoff[tt] + roff * 16);
-              v.x &= xmask[tt];
-              v.y &= xmask[tt];
-              v.z &= xmask[tt];
-              v.w &= xmask[tt];
-            } else {
-              // (no register room for the masks at 3-4 token tiles: 9 warps share 4 register files)
-              v = make_uint4(0u, 0u, 0u, 0u);
-              if (xmask[tt]) v = *reinterpret_cast<const uint4*>(xq + xoff[tt] + roff * 16);
-            }
+            // branch-free: lanes whose token does not exist read token 0's row; their MMA
+            // columns are garbage that is never written out (an output column of the MMA
+            // depends only on its own token column)
+            const uint4 v = *reinterpret_cast<const uint4*>(xq + xoff[tt] + roff * 16);
             // (k0..k7) -> pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7), the weight fragments' K order
             xv[tt] = make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632),
                                 prmt(v.y, v.w, 0x5410), prmt(v.y, v.w, 0x7632));
