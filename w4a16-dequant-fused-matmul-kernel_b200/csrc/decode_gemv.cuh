@@ -242,28 +242,29 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
   uint64_t* empty = full + nst;
   int* flag = reinterpret_cast<int*>(empty + nst);                       // 16 ints
   unsigned long long* ar_peer_smem = reinterpret_cast<unsigned long long*>(flag + 16);   // AR: [8]
+  // this CTA's unit range, worked out once (64-bit divisions) by thread 0:
+  // u0, u1, then c_first, k_first, c_last, k_last and the first CTA of strip c_first
+  long long* range = reinterpret_cast<long long*>(ar_peer_smem + AR_MAX_RANKS);
+  int* range_i = reinterpret_cast<int*>(range + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const long long P = gridDim.x;
   const long long U = p.units;
   const int KS = p.kstages;
-  const long long u0 = unit_begin(blockIdx.x, U, P);
-  const long long u1 = unit_begin(blockIdx.x + 1, U, P);
-  const int c_first = static_cast<int>(u0 / KS);
-  const int k_first = static_cast<int>(u0 - static_cast<long long>(c_first) * KS);
-  const int c_last = static_cast<int>((u1 - 1) / KS);
-  const int k_last = static_cast<int>((u1 - 1) - static_cast<long long>(c_last) * KS);
-  // A strip is "split" when other CTAs hold part of its K range. This CTA owns
-  // its first strip when that strip began in an earlier CTA and ends in this
-  // range; it publishes its last segment when its last strip continues in a
-  // later CTA. (Both can hold; when the range lies inside one strip that began
-  // earlier and continues later, it only publishes.)
-  const bool owns_first = k_first != 0 && (c_last > c_first || k_last == KS - 1);
-  const bool publishes = k_last != KS - 1;
 
   if (threadIdx.x == 0) {
     pdl_launch_dependents();
+    const long long a = unit_begin(blockIdx.x, U, P), b = unit_begin(blockIdx.x + 1, U, P);
+    const int cf = static_cast<int>(a / KS), cl = static_cast<int>((b - 1) / KS);
+    const long long lo = static_cast<long long>(cf) * KS;
+    range[0] = a;
+    range[1] = b;
+    range_i[0] = cf;
+    range_i[1] = static_cast<int>(a - lo);
+    range_i[2] = cl;
+    range_i[3] = static_cast<int>((b - 1) - static_cast<long long>(cl) * KS);
+    range_i[4] = static_cast<int>(((lo + 1) * P + U - 1) / U - 1);
     for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NCW);
@@ -271,6 +272,19 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     mbar_fence_init();
   }
   __syncthreads();
+  const long long u0 = range[0];
+  const long long u1 = range[1];
+  const int c_first = range_i[0];
+  const int k_first = range_i[1];
+  const int c_last = range_i[2];
+  const int k_last = range_i[3];
+  // A strip is "split" when other CTAs hold part of its K range. This CTA owns
+  // its first strip when that strip began in an earlier CTA and ends in this
+  // range; it publishes its last segment when its last strip continues in a
+  // later CTA. (Both can hold; when the range lies inside one strip that began
+  // earlier and continues later, it only publishes.)
+  const bool owns_first = k_first != 0 && (c_last > c_first || k_last == KS - 1);
+  const bool publishes = k_last != KS - 1;
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -508,8 +522,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
   if (owns_first) {
     // y[:, strip c_first] = the pieces of CTAs pf .. this one, summed in CTA order
     const int cs = c_first;
-    const long long lo = static_cast<long long>(cs) * KS;
-    const int pf = static_cast<int>(((lo + 1) * P + U - 1) / U - 1);
+    const int pf = range_i[4];
     const int me = static_cast<int>(blockIdx.x);
     const bool own_parked = c_last > c_first;   // else the strip is the final segment, in red[]
     bool waiting = true;                        // false once this thread's wait budget ran out

@@ -198,7 +198,7 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
   nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
   d.nst = nst;
   d.smem = 1024 + static_cast<size_t>(nst) * sbytes + decode::red_bytes(d.MT) + decode::park_bytes(d.MT) +
-           2 * nst * sizeof(uint64_t) + 64 + 64;
+           2 * nst * sizeof(uint64_t) + 64 + 64 + 64;
   long long grid = static_cast<long long>(dev.num_sms) * decode::ctas_per_sm(d.MT);
   if (grid > d.units) grid = d.units;
   d.grid = static_cast<int>(grid);
