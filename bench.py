@@ -289,48 +289,46 @@ def run_ours(args):
 
     # ---- e2e through the public API with host buffers. Every step copies its x from
     # pinned host memory to the device and reads its y back to pinned host memory.
-    # (a) pipelined, as a serving loop runs its decode steps: copy-in, GEMM and
-    #     copy-out on three streams with double-buffered device x / y (step i+1's x
-    #     lands while step i computes; step i-1's y drains meanwhile), the K steps
-    #     captured in one CUDA graph -- no Python on the timed path;
-    # (b) eager: the same three calls per step from Python on one stream.
+    # (a) pipelined, as a serving loop runs its decode steps, the K steps captured
+    #     in one CUDA graph (no Python on the timed path): each step's x is staged in
+    #     by w4a16.stage_copy -- a kernel, so the GEMM after it still starts under
+    #     programmatic dependent launch (a memory-copy node there would make every
+    #     GEMM wait for the previous one to finish) -- and its y is copied out by a
+    #     memcpy on a second stream while the next steps compute (one device y per
+    #     step, up to a 256 MiB ring, so no GEMM waits on a copy-out);
+    # (b) eager: copy in, GEMM, copy out from Python on one stream.
     Xh = X.cpu().pin_memory()
     Yh = torch.empty(M, N, dtype=torch.float16).pin_memory()
+    y_bytes = M * N * 2
+    ring = max(2, min(args.steps, (256 << 20) // y_bytes))
     Xd = [torch.empty_like(X) for _ in range(2)]
-    Yd = [torch.empty(M, N, device=dev, dtype=torch.float16) for _ in range(2)]
-    s_in = torch.cuda.Stream(device=dev)
+    Yd = [torch.empty(M, N, device=dev, dtype=torch.float16) for _ in range(ring)]
     s_out = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
         for i in range(3):   # warm-up on the GEMM stream (creates its workspace)
-            Xd[i % 2].copy_(Xh, non_blocking=True)
-            w4a16.w4a16_matmul(Xd[i % 2], *copies[i % R], G, out=Yd[i % 2])
-            Yh.copy_(Yd[i % 2], non_blocking=True)
+            w4a16.stage_copy(Xd[i % 2], Xh, src_ready=True)
+            w4a16.w4a16_matmul(Xd[i % 2], *copies[i % R], G, out=Yd[i % ring])
+            Yh.copy_(Yd[i % ring], non_blocking=True)
     torch.cuda.synchronize(dev)
-    in_done = [torch.cuda.Event() for _ in range(2)]
-    k_done = [torch.cuda.Event() for _ in range(2)]
-    out_done = [torch.cuda.Event() for _ in range(2)]
+    k_done = [torch.cuda.Event() for _ in range(ring)]
+    out_done = [torch.cuda.Event() for _ in range(ring)]
     ge = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(ge, stream=stream):
-            s_in.wait_stream(stream)
             s_out.wait_stream(stream)
             for i in range(args.steps):
-                sl = i % 2
-                with torch.cuda.stream(s_in):
-                    if i >= 2:
-                        s_in.wait_event(k_done[sl])      # GEMM i-2 has read Xd[sl]
-                    Xd[sl].copy_(Xh, non_blocking=True)
-                    in_done[sl].record(s_in)
-                stream.wait_event(in_done[sl])
-                if i >= 2:
-                    stream.wait_event(out_done[sl])      # y of step i-2 has left Yd[sl]
-                w4a16.w4a16_matmul(Xd[sl], *copies[i % R], G, out=Yd[sl])
+                sl = i % ring
+                # x of step i from pinned host memory; Xd[i % 2] was last read by GEMM
+                # i-2, which has completed once the copy's wait for GEMM i-1 returns
+                w4a16.stage_copy(Xd[i % 2], Xh, src_ready=True)
+                if i >= ring:
+                    stream.wait_event(out_done[sl])      # y of step i-ring has left Yd[sl]
+                w4a16.w4a16_matmul(Xd[i % 2], *copies[i % R], G, out=Yd[sl])
                 k_done[sl].record(stream)
                 with torch.cuda.stream(s_out):
                     s_out.wait_event(k_done[sl])
                     Yh.copy_(Yd[sl], non_blocking=True)
                     out_done[sl].record(s_out)
-            stream.wait_stream(s_in)
             stream.wait_stream(s_out)
     torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
@@ -350,6 +348,10 @@ def run_ours(args):
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_value = world * step_bytes * args.steps / (float(e2e_t.item()) / 1e3) / 1e9
     del ge
+    # the last step's y, read back through the graph, is the GEMM's result
+    y_last = w4a16.w4a16_matmul(X, *copies[(args.steps - 1) % R], G)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(Yh.to(dev), y_last), "e2e: the y read back differs from the GEMM's result"
 
     for i in range(3):
         Xd[0].copy_(Xh, non_blocking=True)
@@ -397,12 +399,13 @@ def run_ours(args):
                      else "fallback 6650 GB/s",
                      "traffic": traffic,
                      "algorithmic_bytes_per_launch": step_bytes,
-                     "kernel": "decode_gemv_tma_kernel<1>"},
+                     "kernel": "decode_gemv_tma_kernel<1, false>"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": M * K * 2,
                 "d2h_bytes_per_step": M * N * 2,
-                "path": "pinned host X -> w4a16.w4a16_matmul -> pinned host Y every step, pipelined "
-                        "over copy-in / GEMM / copy-out streams with double-buffered device x, y; "
-                        "the K steps replayed from one CUDA graph",
+                "path": "pinned host X -> w4a16.stage_copy -> w4a16.w4a16_matmul -> pinned host Y "
+                        "every step: x staged in by a kernel on the GEMM stream (chains under "
+                        "programmatic dependent launch), y copied out on a second stream while "
+                        "the next steps compute; the K steps replayed from one CUDA graph",
                 "eager": {"value": e2e_eager, "unit": "GB/s",
                           "path": "the same three calls per step from Python on one stream"}},
         "gpu_launches": args.steps,

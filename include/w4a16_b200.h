@@ -100,6 +100,21 @@ int w4a16_swiglu(const void* gate_up, void* h, int64_t M, int64_t N, int64_t ld_
                  int64_t ld_out, void* stream);
 
 /*
+ * dst = src, `bytes` bytes (a multiple of 16; both 16-byte aligned), as a kernel on
+ * `stream` that chains with the GEMM launches around it under programmatic
+ * dependent launch. No reference counterpart: it stages a step's inputs in (or its
+ * outputs out) inside a CUDA-graph-captured serving loop, where a memory-copy node
+ * before a GEMM would make that GEMM wait for its predecessor's completion instead
+ * of overlapping the predecessor's tail. Either pointer may be device memory or
+ * pinned host memory mapped into the device's address space (W4A16_ERR_INVALID
+ * otherwise). src_ready != 0 promises that no earlier kernel on the stream writes
+ * src (e.g. inputs the host wrote into pinned memory): the kernel then reads src
+ * while the previous kernel still runs. dst is written only after the previous
+ * kernel completes, and the copy completes after it.
+ */
+int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* stream);
+
+/*
  * Bytes of workspace w4a16_gemm needs for this shape on the current device
  * (0 for shapes whose kernels need none). No reference counterpart: the
  * reference's kernels never split K across thread blocks.

@@ -251,3 +251,57 @@ def test_column_slices_of_a_wider_output(M, pad):
     assert_gemm_close(np_(buf[:, :2 * N]), np_(full).astype(np.float32), "column slices")
     if pad:
         assert torch.all(buf[:, 2 * N:] == 7.0), "a store landed outside the shards"
+
+
+# ---------------------------- staging copies (w4a16.stage_copy) --------------------
+def test_stage_copy_host_device_and_back():
+    from w4a16 import stage_copy
+    g = torch.Generator().manual_seed(11)
+    src = torch.randint(-2**31, 2**31 - 1, (4096 + 48,), generator=g, dtype=torch.int32).pin_memory()
+    for ready in (True, False):
+        d = torch.empty(src.shape, dtype=torch.int32, device="cuda")
+        stage_copy(d, src, src_ready=ready)
+        torch.cuda.synchronize()
+        assert torch.equal(d.cpu(), src)
+    back = torch.empty_like(src).pin_memory()
+    stage_copy(back, d)
+    d2 = torch.empty_like(d)
+    stage_copy(d2, d)
+    torch.cuda.synchronize()
+    assert torch.equal(back, src) and torch.equal(d2, d)
+
+
+def test_stage_copy_rejects_what_the_device_cannot_reach():
+    from w4a16 import W4A16Error, stage_copy
+    pageable = torch.zeros(64, dtype=torch.int32)   # not pinned: refused before any launch
+    with pytest.raises(W4A16Error):
+        stage_copy(torch.empty(64, dtype=torch.int32, device="cuda"), pageable)
+    with pytest.raises(W4A16Error):   # 8 bytes: not a multiple of 16
+        stage_copy(torch.empty(2, dtype=torch.int32, device="cuda"),
+                   torch.zeros(2, dtype=torch.int32, device="cuda"))
+
+
+def test_stage_copy_then_gemm_replayed_from_a_graph():
+    """x staged in from pinned memory by a kernel, then the decode GEMM, step after
+    step in one CUDA graph: the same bits as the eager GEMM."""
+    from w4a16 import stage_copy
+    X, qw, s, z = _build(1, 4096, 1024, 128, seed=3)
+    Xh = X.cpu().pin_memory()
+    Xd = [torch.empty_like(X) for _ in range(2)]
+    Y = [torch.empty(1, 1024, device="cuda", dtype=torch.float16) for _ in range(6)]
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        stage_copy(Xd[0], Xh, src_ready=True)
+        w4a16_matmul(Xd[0], qw, s, z, 128, out=Y[0])
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(gr, stream=st):
+            for i in range(6):
+                stage_copy(Xd[i % 2], Xh, src_ready=True)
+                w4a16_matmul(Xd[i % 2], qw, s, z, 128, out=Y[i])
+        gr.replay()
+    torch.cuda.synchronize()
+    ref = w4a16_matmul(X, qw, s, z, 128)
+    for i in range(6):
+        assert torch.equal(Y[i], ref), f"step {i}"

@@ -387,6 +387,54 @@ __global__ void swiglu_kernel(const __half* __restrict__ gu, __half* __restrict_
   h[m * ld_out + n] = __float2half_rn(g / (1.0f + expf(-g)) * u);
 }
 
+// dst = src in 16-byte units, as a kernel that chains with the kernels around it
+// under programmatic dependent launch (a memory-copy node in a CUDA graph would
+// make the next GEMM wait for its predecessor's full completion instead). It lets
+// the next kernel launch at once; with src_ready it reads its source before waiting
+// for the previous kernel (the source must not be written by an earlier kernel, e.g.
+// inputs the host placed in pinned memory), otherwise after; it writes only after
+// that wait, so it completes after its predecessor, like the GEMMs.
+constexpr int STAGE_THREADS = 256;
+constexpr int STAGE_PER_THREAD = 4;   // 16-byte units per thread
+__global__ void __launch_bounds__(STAGE_THREADS)
+    stage_kernel(const uint4* src, uint4* dst, int64_t n16, int src_ready) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * STAGE_THREADS * STAGE_PER_THREAD + threadIdx.x;
+  uint4 v[STAGE_PER_THREAD];
+  if (!src_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < STAGE_PER_THREAD; ++i) {
+    const int64_t j = base + static_cast<int64_t>(i) * STAGE_THREADS;
+    if (j < n16) v[i] = src[j];
+  }
+  if (src_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < STAGE_PER_THREAD; ++i) {
+    const int64_t j = base + static_cast<int64_t>(i) * STAGE_THREADS;
+    if (j < n16) dst[j] = v[i];
+  }
+}
+
+// The device address of p when the current device can dereference it (device or
+// managed memory, or pinned host memory mapped into the device's address space),
+// else nullptr.
+const void* device_reachable(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  switch (a.type) {
+    case cudaMemoryTypeDevice:
+    case cudaMemoryTypeManaged:
+      return p;
+    case cudaMemoryTypeHost:
+      return a.devicePointer;
+    default:
+      return nullptr;
+  }
+}
+
 }  // namespace
 }  // namespace w4a16
 
@@ -494,6 +542,39 @@ int w4a16_swiglu(const void* gate_up, void* h, int64_t M, int64_t N, int64_t ld_
   swiglu_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(gate_up), static_cast<__half*>(h), M, N, ld_in, ld_out);
   W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
+}
+
+int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* stream) {
+  if (bytes < 0 || (bytes & 15) != 0) return W4A16_ERR_INVALID;
+  if (bytes == 0) return W4A16_OK;
+  if (src == nullptr || dst == nullptr) return W4A16_ERR_INVALID;
+  if (!aligned16(src) || !aligned16(dst)) return W4A16_ERR_ALIGNMENT;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  const void* s = device_reachable(src);
+  void* d = const_cast<void*>(device_reachable(dst));
+  if (s == nullptr || d == nullptr) return W4A16_ERR_INVALID;
+  const int64_t n16 = bytes / 16;
+  const int64_t per_cta = static_cast<int64_t>(STAGE_THREADS) * STAGE_PER_THREAD;
+  const int64_t blocks = (n16 + per_cta - 1) / per_cta;
+  if (blocks > 0x7fffffffLL) return W4A16_ERR_INVALID;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(STAGE_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, stage_kernel, static_cast<const uint4*>(s), static_cast<uint4*>(d), n16,
+                         src_ready ? 1 : 0) != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_LAUNCH;
+  }
   return W4A16_OK;
 }
 

@@ -155,6 +155,31 @@ def swiglu(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
     return out
 
 
+def stage_copy(dst: Tensor, src: Tensor, src_ready: bool = False) -> Tensor:
+    """``dst.copy_(src)`` as a kernel that chains with the GEMMs around it.
+
+    For loops captured in a CUDA graph: a step's input copied in (or its output
+    copied out) by ``Tensor.copy_`` becomes a memory-copy node, and a GEMM after
+    such a node waits for its predecessor to finish instead of overlapping its
+    tail (programmatic dependent launch). ``dst`` and ``src`` are contiguous
+    tensors of the same size in bytes (a multiple of 16), on the current CUDA
+    device or in pinned host memory. ``src_ready=True`` promises that no earlier
+    kernel on the stream writes ``src`` (e.g. a pinned host buffer the host
+    filled): the copy then reads it while the previous kernel still runs. ``dst``
+    is written after the previous kernel completes. No reference counterpart.
+    """
+    assert dst.is_contiguous() and src.is_contiguous(), "stage_copy needs contiguous tensors"
+    nbytes = src.numel() * src.element_size()
+    assert dst.numel() * dst.element_size() == nbytes, "stage_copy needs equal sizes"
+    dev = dst.device if dst.is_cuda else src.device
+    assert dev.type == "cuda", "stage_copy needs a CUDA tensor on one side"
+    with torch.cuda.device(dev):
+        st = _lib.lib().w4a16_stage(src.data_ptr(), dst.data_ptr(), nbytes, 1 if src_ready else 0,
+                                    _lib.stream_of(dev))
+    _lib.check(st, "w4a16_stage")
+    return dst
+
+
 def w4a16_matmul_into(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
                       y: Tensor, ldy: int, bias: Tensor | None = None) -> None:
     """Low-level variant: write ``Y`` into rows of pitch ``ldy`` starting at
