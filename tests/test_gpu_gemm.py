@@ -70,7 +70,8 @@ def test_matches_reference_grid(M, K, N, group_size):
 
 # ---------------------------- every route and its edges ----------------------------
 @pytest.mark.parametrize("M", [1, 2, 7, 8, 9, 15, 16, 17, 24, 25, 31, 32])
-@pytest.mark.parametrize("K,N,G", [(256, 128, 64), (320, 72, 64), (1024, 264, 256), (576, 1000, 192)])
+@pytest.mark.parametrize("K,N,G", [(256, 128, 64), (320, 72, 64), (1024, 264, 256), (576, 1000, 192),
+                                   (1536, 136, 512), (3072, 128, 1024)])
 def test_decode_route(M, K, N, G):
     X, qw, s, z = _build(M, K, N, G, seed=M * 31 + K)
     assert_gemm_close(np_(w4a16_matmul(X, qw, s, z, G)), _oracle_y(X, qw, s, z, G), f"decode M={M}")
