@@ -92,6 +92,22 @@ struct Params {
   int vec_store;   // y and ldy allow 16-byte stores
 };
 
+// Tile order: groups of RASTER_M row tiles, column-major inside a group, so that a
+// wave of persistent CTAs reads a few row tiles of x (kept in L2) across many weight
+// strips instead of every row tile of x per strip. Up to RASTER_M row tiles (M <=
+// 4096) this is plain column-major order; at M = 8192 the groups measured 6% faster
+// on B200, while groups of 8 were 1% slower at M = 4096.
+constexpr int RASTER_M = 16;
+__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, int& nt) {
+  const int per_group = RASTER_M * p.n_tiles;
+  const int grp = tile / per_group;
+  const int first = grp * RASTER_M;
+  const int gm = p.m_tiles - first < RASTER_M ? p.m_tiles - first : RASTER_M;
+  const int rem = tile - grp * per_group;
+  mt = first + rem % gm;
+  nt = rem / gm;
+}
+
 // Dequantise one packed word (8 consecutive K of one column) into 8 fp16 in
 // natural K order: pairs (k0,k1) (k2,k3) (k4,k5) (k6,k7). Byte b of the word
 // holds nibbles (2b, 2b+1); PRMT copies it into bytes 0 and 2, then one LOP3
@@ -186,7 +202,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       long long issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-        const int m0 = (tile % p.m_tiles) * BM;
+        int mt, nt;
+        tile_coords(p, tile, mt, nt);
+        const int m0 = mt * BM;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u)) { ok = false; break; }
           uint8_t* st = tring + r.slot * T_BYTES;
@@ -259,7 +277,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t s, z;
     };
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-      const int n = (tile / p.m_tiles) * bn + t;
+      int mt, nt;
+      tile_coords(p, tile, mt, nt);
+      const int n = nt * bn + t;
       const bool colok = active && n < p.N;
       auto fetch = [&](int kt, Step& f) {
         if (colok && kt < KT) {
@@ -309,13 +329,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;                 // TMEM lanes this warp may access
     const int h = (warp - EPI_WARP0) >> 2;        // 128-row half of the tile
     uint8_t* stg = staging + (warp - EPI_WARP0) * STG_BYTES;
+    // fp16 chunks (2 KB) alternate between the two halves of the warp's staging
+    // buffer, so a chunk is staged while the previous one's store still reads
+    int half_sel = 0;
+    // y is written once and read by no CTA of this launch: first out of L2, so the
+    // x and weight tiles that other CTAs re-read stay
+    const uint64_t y_policy = l2_evict_first();
     if (p.tma_store && lane == 0) tma_prefetch_desc(&tm_y);
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       if (!warp_wait(accfull, local & 1)) break;
       tc_fence_after();
-      const int n0 = (tile / p.m_tiles) * bn;
-      const int mrow0 = (tile % p.m_tiles) * BM + h * BMH + quarter * 32;
+      int mt, nt;
+      tile_coords(p, tile, mt, nt);
+      const int n0 = nt * bn;
+      const int mrow0 = mt * BM + h * BMH + quarter * 32;
       const int m = mrow0 + lane;
 #pragma unroll 1
       for (int col = 0; col < bn; col += 32) {
@@ -325,13 +353,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (p.tma_store) {
           // Stage the warp's 32 x 32 chunk (row = lane) in the TMA swizzle layout and
           // store it with one bulk tensor copy; rows >= M and columns >= N are clipped.
-          if (lane == 0) bulk_wait_group_read0();   // the previous chunk has left the buffer
+          uint8_t* sb = p.y_f32 ? stg : stg + half_sel * (STG_BYTES / 2);
+          if (lane == 0) {
+            // the chunk that last used this buffer has left it
+            if (p.y_f32) bulk_wait_group_read0();
+            else bulk_wait_group_read1();
+          }
           __syncwarp();
+          half_sel ^= 1;
           if (p.y_f32) {
             // 128-byte rows, 128-byte swizzle: 16-byte chunk c at c ^ (row & 7)
 #pragma unroll
             for (int c = 0; c < 8; ++c)
-              *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+              *reinterpret_cast<uint4*>(sb + lane * 128 + ((c ^ (lane & 7)) << 4)) =
                   make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
           } else {
             uint32_t packed[16];
@@ -352,13 +386,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             // 64-byte rows, 64-byte swizzle: 16-byte chunk c at c ^ ((row >> 1) & 3)
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+              *reinterpret_cast<uint4*>(sb + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
                   make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && mrow0 < p.M && n0 + col < p.N) {
-            tma_store_2d(&tm_y, stg, n0 + col, mrow0);
+            tma_store_2d_hint(&tm_y, sb, n0 + col, mrow0, y_policy);
             bulk_commit_group();
           }
           continue;
