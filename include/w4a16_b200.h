@@ -224,7 +224,25 @@ int w4a16_gemm_allreduce(const void* x, const int32_t* qweight, const void* scal
                          const unsigned long long* peers, int world, int rank,
                          int* ctl, int64_t slot, void* stream);
 
-/* Bytes of one rank's peer-to-peer buffer for w4a16_gemm_allreduce. */
+/*
+ * Column-parallel decode GEMM fused with its all-gather (no counterpart in the
+ * reference): rank r holds columns [r*N, (r+1)*N) of the weight (and of bias) and
+ * every rank receives the whole y = [M, world*N] (row pitch ldy >= world*N): the
+ * CTA that finalises an element writes its fp16 value (bias added, rounded as
+ * w4a16_gemm does) as a tagged 64-bit word into this rank's slot of every rank's
+ * buffer, and the last CTAs to finish copy every rank's slot into y once the tags
+ * of this call are in (bounded wait). The same bits as w4a16_gemm on each rank
+ * followed by an all-gather of the columns. Peers, ctl, slot (>= M*N), ordering
+ * and requirements as w4a16_gemm_allreduce, whose buffers it shares.
+ */
+int w4a16_gemm_allgather(const void* x, const int32_t* qweight, const void* scales,
+                         const void* zeros, const void* bias, void* y,
+                         int64_t M, int64_t N, int64_t K, int64_t group_size,
+                         int64_t ldy, void* workspace, int64_t workspace_bytes,
+                         const unsigned long long* peers, int world, int rank,
+                         int* ctl, int64_t slot, void* stream);
+
+/* Bytes of one rank's peer-to-peer buffer for w4a16_gemm_allreduce / _allgather. */
 int w4a16_p2p_buffer_bytes(int world, int64_t slot, int64_t* bytes_out);
 
 /* A zeroed device buffer of `bytes` on the current device and its 64-byte CUDA

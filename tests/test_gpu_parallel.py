@@ -224,3 +224,98 @@ def test_two_gpu_fused_row_parallel_gemm_allreduce():
     # the ranks agree with each other
     for key in res[0][1]:
         assert np.array_equal(res[0][1][key][0], res[1][1][key][0])
+
+
+def _fused_col_rank(rank: int, world: int, port: int, q) -> None:
+    try:
+        for p in (os.path.join(ROOT, "w4a16-dequant-fused-matmul-kernel_b200"), ROOT,
+                  os.path.join(ROOT, "tests")):
+            sys.path.insert(0, p)
+        import datetime
+        import torch.distributed as dist
+        from helpers import gpu_case as case
+        from w4a16 import _lib, quantize_weight as quant
+        from w4a16.parallel import ColumnParallelW4A16Linear as Col, RowParallelW4A16Linear as Row
+        from w4a16.parallel import close_peer_channels
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        K, N, G = 2048, 1024, 128        # N columns in all, N / world per rank
+        results = {}
+        for M in (1, 5, 32):
+            X, Wd = case(M, K, N, G, sigma=0.05, seed=21 + M, device=dev)
+            qd = quant(Wd, G)
+            bias = (torch.randn(N, generator=torch.Generator(device=dev).manual_seed(4), device=dev)
+                    * 0.1).half()
+            for use_bias in (False, True):
+                fused = Col.from_quantized(*qd, G, bias=bias if use_bias else None)
+                nccl = Col.from_quantized(*qd, G, bias=bias if use_bias else None)
+                nccl.fused_gather = False
+                outs = [fused(X, gather=True) for _ in range(3)]   # several epochs: both halves
+                ref = nccl(X, gather=True)
+                results[(M, use_bias)] = (np_(torch.stack(outs)), np_(ref))
+        # gathers and all-reduces interleaved on one channel (row output = N / world columns)
+        M = 3
+        X, Wd = case(M, K, N, G, sigma=0.05, seed=7, device=dev)
+        col = Col.from_quantized(*quant(Wd, G), G)
+        Xr, Wr = case(M, K, N // world, G, sigma=0.05, seed=8, device=dev)
+        row = Row.from_quantized(*quant(Wr, G), G)
+        row_ref = Row.from_quantized(*quant(Wr, G), G)
+        row_ref.fused_allreduce = False
+        k = K // world
+        xl = Xr[:, rank * k:(rank + 1) * k].contiguous()
+        mixed_ok = True
+        for _ in range(3):
+            yg = col(X, gather=True)
+            yr = row(xl)
+            mixed_ok &= bool(torch.equal(yr, row_ref(xl)))
+            mixed_ok &= bool(torch.equal(yg[:, rank * (N // world):(rank + 1) * (N // world)], col(X)))
+        # the fused gather inside a CUDA graph, replayed
+        eager = col(X, gather=True)
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            col(X, gather=True)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                yg = col(X, gather=True)
+            for _ in range(4):
+                g.replay()
+        torch.cuda.synchronize(dev)
+        graph_ok = bool(torch.equal(yg, eager))
+        flags = _lib.check_device_errors(dev)
+        del g
+        close_peer_channels()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, results, mixed_ok and graph_ok, flags, None))
+    except Exception as e:
+        import traceback
+        q.put((rank, None, None, None, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_fused_column_parallel_gemm_allgather():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_col_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for rank, results, ok, flags, err in res:
+        assert err is None, f"rank {rank}: {err}"
+        assert flags == 0, f"rank {rank}: device error flags {flags}"
+        assert ok, f"rank {rank}: interleaved or graph-replayed calls differ"
+        for (M, use_bias), (outs, ref) in results.items():
+            for i in range(outs.shape[0]):
+                # every column is one rank's fp16 GEMM result: the same bits as NCCL's gather
+                assert np.array_equal(outs[i], ref), f"rank {rank} M={M} bias={use_bias} call {i}"
+    for key in res[0][1]:
+        assert np.array_equal(res[0][1][key][0], res[1][1][key][0])

@@ -95,7 +95,10 @@ struct Params {
   // Fused all-reduce (ar_world > 1): this rank's y is the sum over ranks of every
   // rank's partial GEMM (a row-parallel layer). Each rank owns one peer-to-peer
   // buffer (layout below); ar_peer[q] is rank q's buffer as mapped on this GPU.
+  // Fused all-gather (ar_gather, same buffers): y is [M, ar_world * N], every rank's
+  // columns in rank order; this rank computes columns [ar_rank * N, (ar_rank + 1) * N).
   int ar_world, ar_rank;
+  int ar_gather;
   int ar_tail;                          // CTAs that finish the call: the last ar_tail to arrive
   int* ar_ctl;                          // this rank's control words: [0] epoch, [1] CTAs arrived
   long long ar_slot;                    // elements per rank slot (>= M * N)
@@ -193,8 +196,14 @@ template <bool AR>
 __device__ __forceinline__ void emit(const Params& p, int t, int n, float v, int ar_epoch,
                                      uint32_t peer_s) {
   if (AR) {
-    // the unrounded partial, tagged, into this rank's slot of every rank's buffer
-    // (the peers' first: they are the longer way)
+    // all-reduce: the unrounded partial; all-gather: the final fp16 value (with this
+    // rank's bias), held exactly in fp32. Tagged, into this rank's slot of every rank's
+    // buffer (the peers' first: they are the longer way).
+    if (p.ar_gather) {
+      __half h = __float2half_rn(v);
+      if (p.bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(p.bias[n]));
+      v = __half2float(h);
+    }
     const uint32_t tag = static_cast<uint32_t>(ar_epoch) + 1u;
     const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
     const long long slot0 = (static_cast<long long>(ar_epoch & 1) * p.ar_world + p.ar_rank) * p.ar_slot;
@@ -618,7 +627,38 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     }
     consumer_sync<NCW>();
     const int share = flag[3];
-    if (share >= 0) {
+    if (share >= 0 && p.ar_gather) {
+      // all-gather: y[t, q*N + n] = rank q's word (t, n), for this CTA's share of y
+      const long long NF = static_cast<long long>(p.ar_world) * p.N;
+      const long long total = static_cast<long long>(M) * NF;
+      const long long per = (total + p.ar_tail - 1) / p.ar_tail;
+      const long long lo = share * per;
+      const long long hi = lo + per < total ? lo + per : total;
+      const unsigned long long* half_base =
+          reinterpret_cast<const unsigned long long*>(p.ar_peer[p.ar_rank]) +
+          static_cast<long long>(ar_epoch & 1) * p.ar_world * p.ar_slot;
+      const uint32_t ar_tag = static_cast<uint32_t>(ar_epoch) + 1u;
+      bool waiting = true;   // false once this thread's wait budget ran out
+      for (long long e = lo + ctid; e < hi; e += NCW * 32) {
+        const long long t = e / NF, col = e - t * NF;
+        const long long q = col / p.N, n = col - q * p.N;
+        const unsigned long long* src = half_base + q * p.ar_slot + t * p.N + n;
+        unsigned long long w = ld_volatile_u64(src);
+        uint64_t t0 = 0;
+        for (uint32_t it = 0; waiting && static_cast<uint32_t>(w >> 32) != ar_tag; ++it) {
+          if (it == 0) {
+            t0 = global_timer_ns();
+          } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+            flag_error(kErrWaitTimeout);
+            waiting = false;
+            break;
+          }
+          __nanosleep(32);
+          w = ld_volatile_u64(src);
+        }
+        static_cast<__half*>(p.y)[t * p.ldy + col] = __float2half_rn(__uint_as_float(static_cast<uint32_t>(w)));
+      }
+    } else if (share >= 0) {
       const long long total = static_cast<long long>(M) * p.N;
       const long long per = (total + p.ar_tail - 1) / p.ar_tail;
       const long long lo = share * per;

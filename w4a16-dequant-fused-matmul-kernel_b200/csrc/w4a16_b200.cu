@@ -210,6 +210,7 @@ int plan_decode(DeviceState& dev, int M, int N, int K, DecodePlan* out) {
 // Fused all-reduce arguments of the decode kernel (world 0: off).
 struct ArArgs {
   int world = 0, rank = 0;
+  int gather = 0;                               // 1: all-gather instead of all-reduce
   const unsigned long long* peers = nullptr;   // host array [world]
   int* ctl = nullptr;
   long long slot = 0;
@@ -252,14 +253,15 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.num_stages = d.nst;
   p.ar_world = ar.world;
   p.ar_rank = ar.rank;
+  p.ar_gather = ar.gather;
   p.ar_ctl = ar.ctl;
   p.ar_slot = ar.slot;
   p.ar_tail = 0;
   for (int q = 0; q < decode::AR_MAX_RANKS; ++q) p.ar_peer[q] = q < ar.world ? ar.peers[q] : 0ull;
   if (ar.world > 1) {
-    // enough finishing CTAs that each thread sums AR_ELEMS_PER_THREAD elements
+    // enough finishing CTAs that each thread finishes AR_ELEMS_PER_THREAD output elements
     const long long per_cta = static_cast<long long>(decode::ncw_for(d.MT)) * 32 * decode::AR_ELEMS_PER_THREAD;
-    const long long elems = static_cast<long long>(M) * N;
+    const long long elems = static_cast<long long>(M) * N * (ar.gather ? ar.world : 1);
     const long long tail = (elems + per_cta - 1) / per_cta;
     p.ar_tail = static_cast<int>(tail < 1 ? 1 : (tail > d.grid ? d.grid : tail));
   }
@@ -804,6 +806,43 @@ extern "C" int w4a16_gemm_allreduce(const void* x, const int32_t* qweight, const
   ArArgs ar;
   ar.world = world;
   ar.rank = rank;
+  ar.peers = peers;
+  ar.ctl = ctl;
+  ar.slot = slot;
+  return launch_decode_tma(*dev, static_cast<const __half*>(x), qweight, static_cast<const __half*>(scales),
+                           static_cast<const __half*>(zeros), static_cast<const __half*>(bias), y, 0,
+                           static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                           static_cast<int>(group_size), ldy, workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream), ar);
+}
+
+extern "C" int w4a16_gemm_allgather(const void* x, const int32_t* qweight, const void* scales,
+                                    const void* zeros, const void* bias, void* y, int64_t M, int64_t N,
+                                    int64_t K, int64_t group_size, int64_t ldy, void* workspace,
+                                    int64_t workspace_bytes, const unsigned long long* peers,
+                                    int world, int rank, int* ctl, int64_t slot, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
+  if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
+  if (M > 32 || N % 8 != 0) return W4A16_ERR_INVALID;
+  if (world < 2 || world > decode::AR_MAX_RANKS || rank < 0 || rank >= world) return W4A16_ERR_INVALID;
+  if (ldy < static_cast<int64_t>(world) * N) return W4A16_ERR_INVALID;
+  if (peers == nullptr || ctl == nullptr || slot < M * N) return W4A16_ERR_INVALID;
+  for (int q = 0; q < world; ++q)
+    if (peers[q] == 0ull || (peers[q] & 15ull) != 0ull) return W4A16_ERR_ALIGNMENT;
+  if (M == 0 || N == 0) return W4A16_OK;
+  if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || y == nullptr)
+    return W4A16_ERR_INVALID;
+  if (N > (1ll << 30) || K > (1ll << 30) || (N + decode::BN - 1) / decode::BN > decode::MAX_STRIPS)
+    return W4A16_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales) || !aligned16(zeros))
+    return W4A16_ERR_ALIGNMENT;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  ArArgs ar;
+  ar.world = world;
+  ar.rank = rank;
+  ar.gather = 1;
   ar.peers = peers;
   ar.ctl = ctl;
   ar.slot = slot;

@@ -44,6 +44,9 @@ SIGNATURES = {
     "w4a16_gemm_allreduce": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                               _vp, _c_i64, _vp, ctypes.c_int, ctypes.c_int, _vp, _c_i64, _vp],
                              ctypes.c_int),
+    "w4a16_gemm_allgather": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                              _vp, _c_i64, _vp, ctypes.c_int, ctypes.c_int, _vp, _c_i64, _vp],
+                             ctypes.c_int),
     "w4a16_p2p_buffer_bytes": ([ctypes.c_int, _c_i64, ctypes.POINTER(_c_i64)], ctypes.c_int),
     "w4a16_p2p_alloc": ([_c_i64, ctypes.POINTER(_vp), _vp], ctypes.c_int),
     "w4a16_p2p_open": ([_vp, ctypes.POINTER(_vp)], ctypes.c_int),

@@ -91,6 +91,28 @@ class PeerAllReduce:
         _lib.check(st, "w4a16_gemm_allreduce")
         return y
 
+    def gemm_allgather(self, x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                       zeros: torch.Tensor, group_size: int, bias: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        """fp16 ``[x @ dequant(W_0) | ... | x @ dequant(W_{p-1})]`` (each shard's bias
+        added) for this rank's column shard ``W_r``: the whole output on every rank."""
+        M, K = x.shape
+        N = qweight.shape[1]
+        assert M <= self.max_tokens and N == self.n, "shape outside this channel"
+        assert x.is_contiguous() and x.dtype == torch.float16 and x.device == self.device
+        y = out if out is not None else torch.empty((M, self.world * N), device=x.device, dtype=torch.float16)
+        assert y.is_contiguous() and y.shape == (M, self.world * N)
+        dev = x.device
+        stream = _lib.stream_of(dev)
+        nb = _lib.gemm_workspace_bytes(M, N, K, group_size, dev)
+        ws = _lib.gemm_workspace(nb, dev, stream)
+        st = _lib.lib().w4a16_gemm_allgather(
+            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), _lib.ptr(bias),
+            y.data_ptr(), M, N, K, group_size, self.world * N, _lib.ptr(ws), 0 if ws is None else ws.numel(),
+            self.peers, self.world, self.rank, self.ctl.data_ptr(), self.slot, stream)
+        _lib.check(st, "w4a16_gemm_allgather")
+        return y
+
     def close(self) -> None:
         """Collective: unmap the peers' buffers and free this rank's."""
         if self._own is None:

@@ -8,7 +8,9 @@ schemes the benchmark configurations name:
   slice ``[r*N/p, (r+1)*N/p)`` of qweight / scales / zeros (all N-minor, so
   each shard is a contiguous copy of whole rows). x is replicated; every rank
   computes its slice of y with no communication. Only a caller that needs the
-  full y pays an all-gather (``gather=True``).
+  full y pays an all-gather (``gather=True``): up to 32 tokens the GEMM and the
+  all-gather run as one kernel per rank over NVLink peer memory, larger inputs
+  use NCCL's all-gather.
 * row-parallel (``RowParallelW4A16Linear``): rank r owns the K rows
   ``[r*K/p, (r+1)*K/p)`` (K/p must stay a multiple of the group size) and a
   K-slice of x. Each rank computes unrounded fp32 partial sums, they are
@@ -48,8 +50,9 @@ _peer_channels: dict = {}
 
 
 def _peer_channel(group, device: torch.device, n: int):
-    """The fused GEMM + all-reduce channel for (group, device, n); created on first use
-    (collectively: every rank's first eligible forward reaches here in the same order)."""
+    """The fused GEMM + all-reduce / all-gather channel for (group, device, n) (n: the
+    columns one rank's GEMM computes); created on first use (collectively: every rank's
+    first eligible forward reaches here in the same order)."""
     from .p2p import PeerAllReduce
     key = (id(group), device.index, n)
     ch = _peer_channels.get(key)
@@ -120,10 +123,11 @@ class ColumnParallelW4A16Linear(nn.Module):
     """W4A16 linear layer whose output columns are split across ranks."""
 
     def __init__(self, in_features: int, out_features: int, group_size: int = 128,
-                 bias: bool = True, device=None, group=None) -> None:
+                 bias: bool = True, device=None, group=None, fused_gather: bool = True) -> None:
         super().__init__()
         self.group = group
         self.rank, self.world = _world(group)
+        self.fused_gather = fused_gather
         if in_features % 8 != 0 or in_features % group_size != 0:
             raise ValueError(f"in_features={in_features} must be divisible by 8 and group_size={group_size}")
         if out_features % self.world != 0:
@@ -151,6 +155,12 @@ class ColumnParallelW4A16Linear(nn.Module):
         return mod
 
     def forward(self, x: Tensor, gather: bool = False) -> Tensor:
+        from .p2p import MAX_TOKENS
+        n = self.out_features // self.world
+        if (gather and self.world > 1 and self.fused_gather and x.is_cuda and x.dim() == 2
+                and x.shape[0] <= MAX_TOKENS and n % 8 == 0 and x.is_contiguous()):
+            ch = _peer_channel(self.group, x.device, n)
+            return ch.gemm_allgather(x, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias)
         y = w4a16_matmul(x, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias)
         return gather_columns(y, self.group) if gather else y
 
