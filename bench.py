@@ -165,14 +165,26 @@ def cpu_inputs(cfg, seed=0):
     return X, qw, s, z
 
 
-def time_cpu(cfg, min_seconds=10.0, max_iters=50, steps=None):
+def cpu_model() -> str:
+    """The host CPU's model name (Linux), for the baseline's record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def time_cpu(cfg, min_seconds=10.0, max_iters=50, steps=None, threads=None):
     """Time the CPU path; returns (median seconds per GEMM, iterations, threads).
 
     Runs for at least ``min_seconds`` (bounded by ``max_iters``) or exactly
     ``steps`` iterations. BLAS is pinned to one thread per worker; the column
-    blocks give the parallelism."""
+    blocks give the parallelism (all host cores unless ``threads`` is given)."""
     from threadpoolctl import threadpool_limits
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     X, qw, s, z = cpu_inputs(cfg)
     times = []
     with threadpool_limits(limits=1):
@@ -204,7 +216,8 @@ def run_reference(args):
                                         "M": 1, "K": 4096, "N": 11008, "group_size": 128},
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{n} full decode GEMMs (dequantise-then-matmul), "
-                                   f"numpy oracle over {threads} column blocks"},
+                                   f"numpy oracle over {threads} column blocks",
+                         "cpu_model": cpu_model()},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -416,9 +429,14 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         t_cpu, n_cpu, threads = time_cpu(DECODE, min_seconds=args.cpu_seconds)
         cpu_gbs = step_bytes / t_cpu / 1e9
+        t_one, n_one, _ = time_cpu(DECODE, steps=3, threads=1)
         line["cpu_baseline"] = {"value": cpu_gbs, "unit": "GB/s", "cores": threads, "kind": "port",
                                 "sample": f"{n_cpu} full decode GEMMs (dequantise-then-matmul, numpy oracle "
-                                          f"over {threads} column blocks), median {t_cpu * 1e3:.1f} ms"}
+                                          f"over {threads} column blocks), median {t_cpu * 1e3:.1f} ms",
+                                "cpu_model": cpu_model(),
+                                "one_core": {"value": step_bytes / t_one / 1e9, "unit": "GB/s",
+                                             "sample": f"{n_one} full decode GEMMs on 1 thread, median "
+                                                       f"{t_one * 1e3:.1f} ms"}}
     if rank == 0:
         print(json.dumps(line), flush=True)
     del g
