@@ -1,14 +1,16 @@
-"""Peer-to-peer all-reduce channel for row-parallel decode GEMMs.
+"""Peer-to-peer channel for tensor-parallel decode GEMMs fused with their collective.
 
 ``PeerAllReduce`` owns, on every rank of a process group, one CUDA IPC buffer
 mapped on every other rank (plain peer memory over NVLink / NVSwitch; no
-multicast object), the list of those mappings and two device control words. A
-call runs ``w4a16_gemm_allreduce``: one kernel per rank computes its partial
-GEMM and writes each finished fp32 element, tagged with the call's epoch, into
-every rank's buffer; its last CTAs wait for every rank's tagged elements of
-their share and sum them in rank order -- the GEMM and the all-reduce of a
-row-parallel layer in one launch, with the same result as an fp32 all-reduce
-followed by one fp16 rounding.
+multicast object), the list of those mappings and two device control words.
+``gemm`` runs ``w4a16_gemm_allreduce`` (row-parallel: one kernel per rank
+computes its partial GEMM and writes each finished fp32 element, tagged with the
+call's epoch, into every rank's buffer; its last CTAs wait for every rank's
+tagged elements of their share and sum them in rank order -- the same result as
+an fp32 all-reduce followed by one fp16 rounding). ``gemm_allgather`` runs
+``w4a16_gemm_allgather`` (column-parallel: the finished fp16 elements are
+exchanged the same way and placed, so every rank receives the whole output --
+the same bits as the GEMM followed by an all-gather).
 
 Creating a channel is collective (every rank of the group, same order, same
 arguments); so is every call. Calls on one channel must be issued on one
