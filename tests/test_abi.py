@@ -79,3 +79,28 @@ def test_quantize_rejects_bad_arguments_without_a_device():
 def test_check_device_errors_signature():
     fn = _lib.lib().w4a16_check_device_errors
     assert fn.argtypes[1] == ctypes.POINTER(ctypes.c_uint32)
+
+
+@pytest.mark.parametrize("fn", ["w4a16_gemm_allreduce", "w4a16_gemm_allgather"])
+@pytest.mark.parametrize("M,N,ldy,world,rank", [
+    (33, 64, 128, 2, 0),            # more than 32 tokens
+    (1, 60, 128, 2, 0),             # N % 8
+    (1, 64, 128, 1, 0),             # one rank
+    (1, 64, 128, 9, 0),             # more ranks than the buffers hold
+    (1, 64, 128, 2, 2),             # rank outside the group
+    (32, 1 << 28, 1 << 29, 2, 0),   # output beyond the finishing CTAs' 32-bit indices
+])
+def test_fused_collectives_reject_bad_arguments_without_a_device(fn, M, N, ldy, world, rank):
+    lib = _lib.lib()
+    peers = (ctypes.c_ulonglong * 8)()
+    st = getattr(lib, fn)(None, None, None, None, None, None, M, N, 128, 64, ldy, None, 0,
+                          peers, world, rank, None, M * N, None)
+    assert st == -1   # W4A16_ERR_INVALID, before any device work
+
+
+def test_allgather_needs_room_for_every_rank():
+    lib = _lib.lib()
+    peers = (ctypes.c_ulonglong * 8)()
+    # y rows of 64 columns cannot hold 2 ranks x 64 columns
+    assert lib.w4a16_gemm_allgather(None, None, None, None, None, None, 1, 64, 128, 64, 64, None, 0,
+                                    peers, 2, 0, None, 64, None) == -1

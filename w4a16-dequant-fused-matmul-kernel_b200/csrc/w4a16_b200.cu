@@ -790,6 +790,7 @@ extern "C" int w4a16_gemm_allreduce(const void* x, const int32_t* qweight, const
   if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
   if (ldy < N || M > 32 || N % 8 != 0) return W4A16_ERR_INVALID;
   if (world < 2 || world > decode::AR_MAX_RANKS || rank < 0 || rank >= world) return W4A16_ERR_INVALID;
+  if (M * N > 0x7fffffffLL) return W4A16_ERR_INVALID;   // the finishing CTAs index y in 32 bits
   if (peers == nullptr || ctl == nullptr || slot < M * N) return W4A16_ERR_INVALID;
   for (int q = 0; q < world; ++q)
     if (peers[q] == 0ull || (peers[q] & 15ull) != 0ull) return W4A16_ERR_ALIGNMENT;
@@ -826,6 +827,7 @@ extern "C" int w4a16_gemm_allgather(const void* x, const int32_t* qweight, const
   if (M > 32 || N % 8 != 0) return W4A16_ERR_INVALID;
   if (world < 2 || world > decode::AR_MAX_RANKS || rank < 0 || rank >= world) return W4A16_ERR_INVALID;
   if (ldy < static_cast<int64_t>(world) * N) return W4A16_ERR_INVALID;
+  if (M * world * N > 0x7fffffffLL) return W4A16_ERR_INVALID;   // 32-bit indices into y
   if (peers == nullptr || ctl == nullptr || slot < M * N) return W4A16_ERR_INVALID;
   for (int q = 0; q < world; ++q)
     if (peers[q] == 0ull || (peers[q] & 15ull) != 0ull) return W4A16_ERR_ALIGNMENT;
