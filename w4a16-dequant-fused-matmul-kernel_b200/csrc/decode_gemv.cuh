@@ -629,20 +629,23 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     const int share = flag[3];
     if (share >= 0 && p.ar_gather) {
       // all-gather: y[t, q*N + n] = rank q's word (t, n), for this CTA's share of y
-      const long long NF = static_cast<long long>(p.ar_world) * p.N;
-      const long long total = static_cast<long long>(M) * NF;
-      const long long per = (total + p.ar_tail - 1) / p.ar_tail;
-      const long long lo = share * per;
-      const long long hi = lo + per < total ? lo + per : total;
+      // (32-bit indices: the host keeps M * world * N below 2^31; a thread's element
+      // indices advance by the stride without divisions)
+      const int NF = p.ar_world * p.N;
+      const int total = M * NF;
+      const int per = (total + p.ar_tail - 1) / p.ar_tail;
+      const int lo = share * per;
+      const int hi = lo + per < total ? lo + per : total;
       const unsigned long long* half_base =
           reinterpret_cast<const unsigned long long*>(p.ar_peer[p.ar_rank]) +
           static_cast<long long>(ar_epoch & 1) * p.ar_world * p.ar_slot;
       const uint32_t ar_tag = static_cast<uint32_t>(ar_epoch) + 1u;
       bool waiting = true;   // false once this thread's wait budget ran out
-      for (long long e = lo + ctid; e < hi; e += NCW * 32) {
-        const long long t = e / NF, col = e - t * NF;
-        const long long q = col / p.N, n = col - q * p.N;
-        const unsigned long long* src = half_base + q * p.ar_slot + t * p.N + n;
+      int t = (lo + ctid) / NF, q = (lo + ctid - t * NF) / p.N;
+      int n = lo + ctid - t * NF - q * p.N;
+      for (int e = lo + ctid; e < hi; e += NCW * 32) {
+        const int col = q * p.N + n;
+        const unsigned long long* src = half_base + static_cast<long long>(q) * p.ar_slot + t * p.N + n;
         unsigned long long w = ld_volatile_u64(src);
         uint64_t t0 = 0;
         for (uint32_t it = 0; waiting && static_cast<uint32_t>(w >> 32) != ar_tag; ++it) {
@@ -656,19 +659,28 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           __nanosleep(32);
           w = ld_volatile_u64(src);
         }
-        static_cast<__half*>(p.y)[t * p.ldy + col] = __float2half_rn(__uint_as_float(static_cast<uint32_t>(w)));
+        static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + col] =
+            __float2half_rn(__uint_as_float(static_cast<uint32_t>(w)));
+        for (n += NCW * 32; n >= p.N; n -= p.N) {
+          if (++q == p.ar_world) {
+            q = 0;
+            ++t;
+          }
+        }
       }
     } else if (share >= 0) {
-      const long long total = static_cast<long long>(M) * p.N;
-      const long long per = (total + p.ar_tail - 1) / p.ar_tail;
-      const long long lo = share * per;
-      const long long hi = lo + per < total ? lo + per : total;
+      // (32-bit indices: the host keeps M * N below 2^31)
+      const int total = M * p.N;
+      const int per = (total + p.ar_tail - 1) / p.ar_tail;
+      const int lo = share * per;
+      const int hi = lo + per < total ? lo + per : total;
       const unsigned long long* half_base =
           reinterpret_cast<const unsigned long long*>(p.ar_peer[p.ar_rank]) +
           static_cast<long long>(ar_epoch & 1) * p.ar_world * p.ar_slot;
       const uint32_t ar_tag = static_cast<uint32_t>(ar_epoch) + 1u;
       bool waiting = true;   // false once this thread's wait budget ran out
-      for (long long e = lo + ctid; e < hi; e += NCW * 32) {
+      int t = (lo + ctid) / p.N, n = lo + ctid - t * p.N;
+      for (int e = lo + ctid; e < hi; e += NCW * 32) {
         unsigned long long w[AR_MAX_RANKS];
 #pragma unroll
         for (int q = 0; q < AR_MAX_RANKS; ++q)
@@ -693,10 +705,10 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           a = q == 0 ? v : a + v;   // rank order
         }
         // y = fp16(sum) [+ bias, rounded again]
-        const int t = static_cast<int>(e / p.N), n = static_cast<int>(e - static_cast<long long>(t) * p.N);
         __half h = __float2half_rn(a);
         if (p.bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(p.bias[n]));
         static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + n] = h;
+        for (n += NCW * 32; n >= p.N; n -= p.N) ++t;
       }
     }
   }
