@@ -628,12 +628,15 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     consumer_sync<NCW>();
     const int share = flag[3];
     if (share >= 0 && p.ar_gather) {
-      // all-gather: y[t, q*N + n] = rank q's word (t, n), for this CTA's share of y
-      // (32-bit indices: the host keeps M * world * N below 2^31; a thread's element
-      // indices advance by the stride without divisions)
+      // all-gather: y[t, q*N + n] = rank q's word (t, n), for this CTA's share of y.
+      // A thread takes 4 consecutive elements per step (N % 8 == 0 keeps them in one
+      // rank's row segment; shares start on multiples of 4) and issues their 4 loads
+      // before polling any of them. (32-bit indices: the host keeps M * world * N
+      // below 2^31; a thread's indices advance by the stride without divisions.)
+      constexpr int VE = 4;
       const int NF = p.ar_world * p.N;
       const int total = M * NF;
-      const int per = (total + p.ar_tail - 1) / p.ar_tail;
+      const int per = ((total + p.ar_tail - 1) / p.ar_tail + VE - 1) / VE * VE;
       const int lo = share * per;
       const int hi = lo + per < total ? lo + per : total;
       const unsigned long long* half_base =
@@ -641,27 +644,34 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           static_cast<long long>(ar_epoch & 1) * p.ar_world * p.ar_slot;
       const uint32_t ar_tag = static_cast<uint32_t>(ar_epoch) + 1u;
       bool waiting = true;   // false once this thread's wait budget ran out
-      int t = (lo + ctid) / NF, q = (lo + ctid - t * NF) / p.N;
-      int n = lo + ctid - t * NF - q * p.N;
-      for (int e = lo + ctid; e < hi; e += NCW * 32) {
+      const int e0 = lo + VE * ctid;
+      int t = e0 / NF, q = (e0 - t * NF) / p.N;
+      int n = e0 - t * NF - q * p.N;
+      for (int e = e0; e < hi; e += VE * NCW * 32) {
         const int col = q * p.N + n;
         const unsigned long long* src = half_base + static_cast<long long>(q) * p.ar_slot + t * p.N + n;
-        unsigned long long w = ld_volatile_u64(src);
-        uint64_t t0 = 0;
-        for (uint32_t it = 0; waiting && static_cast<uint32_t>(w >> 32) != ar_tag; ++it) {
-          if (it == 0) {
-            t0 = global_timer_ns();
-          } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
-            flag_error(kErrWaitTimeout);
-            waiting = false;
-            break;
+        unsigned long long w[VE];
+#pragma unroll
+        for (int v = 0; v < VE; ++v) w[v] = ld_volatile_u64(src + v);
+#pragma unroll
+        for (int v = 0; v < VE; ++v) {
+          uint64_t t0 = 0;
+          for (uint32_t it = 0; waiting && static_cast<uint32_t>(w[v] >> 32) != ar_tag; ++it) {
+            if (it == 0) {
+              t0 = global_timer_ns();
+            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+              flag_error(kErrWaitTimeout);
+              waiting = false;
+              break;
+            }
+            __nanosleep(32);
+            w[v] = ld_volatile_u64(src + v);
           }
-          __nanosleep(32);
-          w = ld_volatile_u64(src);
         }
-        static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + col] =
-            __float2half_rn(__uint_as_float(static_cast<uint32_t>(w)));
-        for (n += NCW * 32; n >= p.N; n -= p.N) {
+        __half* yrow = static_cast<__half*>(p.y) + static_cast<long long>(t) * p.ldy + col;
+#pragma unroll
+        for (int v = 0; v < VE; ++v) yrow[v] = __float2half_rn(__uint_as_float(static_cast<uint32_t>(w[v])));
+        for (n += VE * NCW * 32; n >= p.N; n -= p.N) {
           if (++q == p.ar_world) {
             q = 0;
             ++t;
