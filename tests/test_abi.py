@@ -104,3 +104,19 @@ def test_allgather_needs_room_for_every_rank():
     # y rows of 64 columns cannot hold 2 ranks x 64 columns
     assert lib.w4a16_gemm_allgather(None, None, None, None, None, None, 1, 64, 128, 64, 64, None, 0,
                                     peers, 2, 0, None, 64, None) == -1
+
+
+@pytest.mark.parametrize("nbytes,src,dst", [
+    (24, 16, 16),     # not a multiple of 16 bytes
+    (-16, 16, 16),    # negative size
+    (32, None, 16),   # no source
+    (32, 16, None),   # no destination
+])
+def test_stage_rejects_bad_arguments_without_a_device(nbytes, src, dst):
+    st = _lib.lib().w4a16_stage(src, dst, nbytes, 1, None)
+    assert st == -1   # W4A16_ERR_INVALID, before any device work
+
+
+def test_stage_rejects_misaligned_pointers_without_a_device():
+    assert _lib.lib().w4a16_stage(8, 16, 32, 0, None) == -2   # W4A16_ERR_ALIGNMENT
+    assert _lib.lib().w4a16_stage(16, 0, 0, 0, None) == 0      # nothing to copy
