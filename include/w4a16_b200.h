@@ -155,12 +155,37 @@ int w4a16_dequantize(const int32_t* qweight, const void* scales, const void* zer
 
 /*
  * Read and clear the device's sticky error flags for the current device
- * (bit 0: a pipeline wait in a GEMM kernel ran out of its iteration budget
- * and the kernel abandoned its tile). Synchronises the given stream.
- * Returns W4A16_OK when no flag was set, W4A16_ERR_TIMEOUT when one was.
+ * (bit 0: a bounded wait in a GEMM kernel ran out of its time budget and the
+ * kernel abandoned its tile). Synchronises the given stream.
+ * Returns W4A16_OK when no flag was set, W4A16_ERR_TIMEOUT when one was; in
+ * that case it also zeroes this device's w4a16_gemm_noalloc scratch array (if
+ * it has been set up) on `stream` and synchronises again, since its callers
+ * cannot clear it themselves. Results of the launches since the last check are
+ * unspecified after a timeout. Caller-owned workspaces and peer buffers may
+ * hold stale words too: zero them (w4a16_reset_scratch) before reusing them.
  * No reference counterpart: the reference's kernels have no bounded waits.
  */
 int w4a16_check_device_errors(void* stream, uint32_t* flags_out);
+
+/*
+ * Time budget, in nanoseconds, of every bounded wait in the kernels launched
+ * after this call (process-wide; 0 restores the default of 4 s; otherwise
+ * 1 ms <= ns <= 600 s, else W4A16_ERR_INVALID). Each launch carries the budget
+ * as a kernel parameter, so launches already queued or captured in a CUDA graph
+ * keep theirs. A shorter budget lets a caller (or a test) detect a lost peer
+ * sooner; legitimate waits last microseconds to milliseconds. The waits that
+ * keep a kernel from exiting with copies or MMAs in flight always use 4 s.
+ * No reference counterpart.
+ */
+int w4a16_set_wait_budget_ns(int64_t ns);
+
+/*
+ * After W4A16_ERR_TIMEOUT: zero `workspace_bytes` of a caller's GEMM workspace
+ * (when `workspace` is not NULL) and this device's w4a16_gemm_noalloc scratch
+ * array (when set up), asynchronously on `stream`; allocates nothing. The next
+ * GEMM on that stream then starts from clean scratch. No reference counterpart.
+ */
+int w4a16_reset_scratch(void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * w4a16_gemm without a workspace argument and without allocating anything.
@@ -181,8 +206,10 @@ int w4a16_check_device_errors(void* stream, uint32_t* flags_out);
  * zeroes it on `stream` and synchronises that stream. Make that first call
  * before any stream capture; a first call made while `stream` is capturing
  * returns W4A16_ERR_INVALID. The array must be zero whenever a decode launch
- * starts: set-up zeroes it and every completed launch leaves it zero, but a
- * launch abandoned on W4A16_ERR_TIMEOUT may not. There is ONE scratch array per device, so calls whose kernels can run
+ * starts: set-up zeroes it and every completed launch leaves it zero; a launch
+ * abandoned on a timeout may leave words set, and w4a16_check_device_errors
+ * zeroes the array again when it reports W4A16_ERR_TIMEOUT (as does
+ * w4a16_reset_scratch). There is ONE scratch array per device, so calls whose kernels can run
  * at the same time (different streams, threads or processes sharing a
  * context, parallel graph branches) race on it and give wrong results: keep
  * every call on one device ordered, or use w4a16_gemm with a workspace per

@@ -120,3 +120,18 @@ def test_stage_rejects_bad_arguments_without_a_device(nbytes, src, dst):
 def test_stage_rejects_misaligned_pointers_without_a_device():
     assert _lib.lib().w4a16_stage(8, 16, 32, 0, None) == -2   # W4A16_ERR_ALIGNMENT
     assert _lib.lib().w4a16_stage(16, 0, 0, 0, None) == 0      # nothing to copy
+
+
+def test_wait_budget_setter_validates_without_a_device():
+    lib = _lib.lib()
+    assert lib.w4a16_set_wait_budget_ns(-1) == -1
+    assert lib.w4a16_set_wait_budget_ns(999_999) == -1           # below 1 ms
+    assert lib.w4a16_set_wait_budget_ns(601 * 10**9) == -1       # above 600 s
+    assert lib.w4a16_set_wait_budget_ns(20_000_000) == 0
+    assert lib.w4a16_set_wait_budget_ns(0) == 0                  # back to the default
+
+
+def test_reset_scratch_rejects_bad_arguments_without_a_device():
+    lib = _lib.lib()
+    assert lib.w4a16_reset_scratch(None, 16, None) == -1
+    assert lib.w4a16_reset_scratch(None, -1, None) == -1

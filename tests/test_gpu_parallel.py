@@ -110,7 +110,7 @@ def _nccl_rank(rank: int, world: int, port: int, q) -> None:
         mlp = MLP.from_dense(Wg, Wu, Wd, G)(X)
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, col_err, mlp.cpu().numpy(), None))
+        q.put((rank, (col_err, y.cpu().numpy()), mlp.cpu().numpy(), None))
     except Exception as e:
         q.put((rank, None, None, repr(e)))
 
@@ -126,15 +126,19 @@ def test_two_gpu_column_gather_and_mlp():
     res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
     for p in procs:
         p.join(timeout=60)
-    for rank, col_err, _, err in res:
+    for rank, col, _, err in res:
         assert err is None, f"rank {rank}: {err}"
-        assert col_err <= 1e-2, f"rank {rank}: gathered shards differ by {col_err}"
+        assert col[0] <= 1e-2, f"rank {rank}: gathered shards differ by {col[0]}"
     # the same block unsharded on one GPU
     D, H, G, M = 1024, 2048, 128, 4
     X, Wg = gpu_case(M, D, H, G, sigma=0.05, seed=1)
     _, Wu = gpu_case(1, D, H, G, sigma=0.05, seed=2)
     _, Wd = gpu_case(1, H, D, G, sigma=0.05, seed=3)
-    ref = _mlp_oracle(X, quantize_weight(Wg, G), quantize_weight(Wu, G), quantize_weight(Wd, G), G)
+    qg = quantize_weight(Wg, G)
+    col_ref = oracle.reference_w4a16(np_(X), *(np_(t) for t in qg), G)
+    for rank, col, _, _ in res:
+        assert_gemm_close(col[1], col_ref, f"NCCL column gather vs oracle, rank {rank}")
+    ref = _mlp_oracle(X, qg, quantize_weight(Wu, G), quantize_weight(Wd, G), G)
     for rank, _, y, _ in res:
         assert_gemm_close(y, ref, f"tp mlp rank {rank}")
 
@@ -224,6 +228,18 @@ def test_two_gpu_fused_row_parallel_gemm_allreduce():
     # the ranks agree with each other
     for key in res[0][1]:
         assert np.array_equal(res[0][1][key][0], res[1][1][key][0])
+    # and with the oracle of the unsharded layer (rebuilt here from the same seeds)
+    K, N, G = 2048, 1024, 128
+    for (M, use_bias), (outs, _) in res[0][1].items():
+        X, Wd = gpu_case(M, K, N, G, sigma=0.05, seed=11 + M)
+        qd = quantize_weight(Wd, G)
+        ref = oracle.reference_w4a16(np_(X), *(np_(t) for t in qd), G)
+        if use_bias:
+            bias = (torch.randn(N, generator=torch.Generator(device="cuda").manual_seed(3), device="cuda")
+                    * 0.1).half()
+            ref = (ref + np_(bias)).astype(np.float16)
+        for i in range(outs.shape[0]):
+            assert_gemm_close(outs[i], ref, f"fused all-reduce vs oracle M={M} bias={use_bias} call {i}")
 
 
 def _fused_col_rank(rank: int, world: int, port: int, q) -> None:
@@ -319,3 +335,15 @@ def test_two_gpu_fused_column_parallel_gemm_allgather():
                 assert np.array_equal(outs[i], ref), f"rank {rank} M={M} bias={use_bias} call {i}"
     for key in res[0][1]:
         assert np.array_equal(res[0][1][key][0], res[1][1][key][0])
+    # and with the oracle of the unsharded layer (rebuilt here from the same seeds)
+    K, N, G = 2048, 1024, 128
+    for (M, use_bias), (outs, _) in res[0][1].items():
+        X, Wd = gpu_case(M, K, N, G, sigma=0.05, seed=21 + M)
+        qd = quantize_weight(Wd, G)
+        ref = oracle.reference_w4a16(np_(X), *(np_(t) for t in qd), G)
+        if use_bias:
+            bias = (torch.randn(N, generator=torch.Generator(device="cuda").manual_seed(4), device="cuda")
+                    * 0.1).half()
+            ref = (ref + np_(bias)).astype(np.float16)
+        for i in range(outs.shape[0]):
+            assert_gemm_close(outs[i], ref, f"fused all-gather vs oracle M={M} bias={use_bias} call {i}")

@@ -21,10 +21,12 @@ namespace w4a16 {
 constexpr uint32_t kErrWaitTimeout = 1u;
 __device__ uint32_t g_device_error = 0;
 
-// Time budget of one mbarrier wait, in nanoseconds of %globaltimer. Every
+// Default time budget of one bounded wait, in nanoseconds of %globaltimer. Every
 // legitimate wait in these kernels is bounded by one CTA's own pipeline (at
-// most milliseconds even for very long K), so 4 s only expires on a lost
-// wait, while still allowing for time-slicing with other contexts.
+// most milliseconds even for very long K) or by the peers' matching launches, so
+// 4 s only expires on a lost wait, while still allowing for time-slicing with
+// other contexts. The host passes the budget to every launch (kernel parameter),
+// so a caller can shorten it (w4a16_set_wait_budget_ns).
 constexpr uint64_t kWaitBudgetNs = 4ull * 1000ull * 1000ull * 1000ull;
 
 __device__ __forceinline__ void flag_error(uint32_t bits) {
@@ -127,13 +129,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed. Returns false (and
-// raises the sticky error bit) when the time budget runs out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// raises the sticky error bit) when `budget_ns` of %globaltimer runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t budget_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 7u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) break;
+    if ((i & 7u) == 0u && global_timer_ns() - t0 > budget_ns) break;
   }
   flag_error(kErrWaitTimeout);
   return false;

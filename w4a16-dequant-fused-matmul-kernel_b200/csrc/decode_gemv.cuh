@@ -103,6 +103,7 @@ struct Params {
   int* ar_ctl;                          // this rank's control words: [0] epoch, [1] CTAs arrived
   long long ar_slot;                    // elements per rank slot (>= M * N)
   unsigned long long ar_peer[8];        // [ar_world] buffer addresses (kernel parameters)
+  unsigned long long wait_ns;           // budget of every bounded wait (%globaltimer ns)
 };
 
 // Peer-to-peer all-reduce buffer (one per rank): two halves, selected by the
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
       uint32_t ph = pre == nst ? 1u : 0u;
       long long issued = pre;
       for (long long u = u0 + pre; u < u1; ++u, ++issued) {
-        if (!mbar_wait(&empty[s], ph ^ 1)) break;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.wait_ns)) break;
         uint8_t* st = smem + s * sbytes;
         const int grow = p.g_shift >= 0 ? (k * KSTAGE) >> p.g_shift : (k * KSTAGE) / p.G;
         mbar_arrive_expect_tx(&full[s], sbytes);
@@ -341,12 +342,13 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
         if (++s == nst) { s = 0; ph ^= 1; }
         if (++k == KS) { k = 0; ++c; }
       }
-      // Never leave with copies in flight: wait for the newest stage of every slot.
+      // Never leave with copies in flight: wait for the newest stage of every slot
+      // (with the default budget, whatever budget the caller chose for the pipeline).
       const long long n_in_flight = issued < nst ? issued : nst;
       for (long long i = 0; i < n_in_flight; ++i) {
         if (s == 0) { s = nst; ph ^= 1; }
         --s;
-        mbar_wait(&full[s], ph);
+        mbar_wait(&full[s], ph, kWaitBudgetNs);
       }
     }
     return;   // takes no part in the consumers' barriers below
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     }
     if (ok) {
       bool got = true;
-      if (lane == 0) got = mbar_wait(&full[s], ph);
+      if (lane == 0) got = mbar_wait(&full[s], ph, p.wait_ns);
       ok = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
       __syncwarp();   // orders the other lanes' shared-memory reads after lane 0's acquire
     }
@@ -588,7 +590,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           for (uint32_t it = 0; waiting && (w[i] >> 32) != 1ull; ++it) {
             if (it == 0) {
               t0 = global_timer_ns();
-            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > p.wait_ns) {
               flag_error(kErrWaitTimeout);
               waiting = false;
               break;
@@ -659,7 +661,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           for (uint32_t it = 0; waiting && static_cast<uint32_t>(w[v] >> 32) != ar_tag; ++it) {
             if (it == 0) {
               t0 = global_timer_ns();
-            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > p.wait_ns) {
               flag_error(kErrWaitTimeout);
               waiting = false;
               break;
@@ -703,7 +705,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
           for (uint32_t it = 0; waiting && static_cast<uint32_t>(w[q] >> 32) != ar_tag; ++it) {
             if (it == 0) {
               t0 = global_timer_ns();
-            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > kWaitBudgetNs) {
+            } else if ((it & 15u) == 0u && global_timer_ns() - t0 > p.wait_ns) {
               flag_error(kErrWaitTimeout);
               waiting = false;
               break;

@@ -90,6 +90,7 @@ struct Params {
   int bn;          // tile columns
   uint32_t idesc;  // tcgen05 instruction descriptor for M=128, N=bn
   int vec_store;   // y and ldy allow 16-byte stores
+  unsigned long long wait_ns;   // budget of every bounded wait (%globaltimer ns)
 };
 
 // Tile order: groups of RASTER_M row tiles, column-major inside a group, so that a
@@ -130,9 +131,9 @@ __device__ __forceinline__ uint4 dequant_word_nat(uint32_t w, uint32_t zc, uint3
 }
 
 // Lane 0 waits, the warp follows: keeps mbarrier polling off the shared-memory pipe.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint64_t budget_ns) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity);
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, budget_ns);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   __syncwarp();
   return ok;
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tile_coords(p, tile, mt, nt);
         const int m0 = mt * BM;
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u)) { ok = false; break; }
+          if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u, p.wait_ns)) { ok = false; break; }
           uint8_t* st = tring + r.slot * T_BYTES;
           mbar_arrive_expect_tx(&tfull[r.slot], A_BYTES);
           tma_load_2d(st, &tm_x, &tfull[r.slot], kt * BK, m0);
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (long long i = 0; i < n; ++i) {
         if (r.slot == 0) { r.slot = TSTAGES; r.phase ^= 1u; }
         --r.slot;
-        mbar_wait(&tfull[r.slot], r.phase);
+        mbar_wait(&tfull[r.slot], r.phase, kWaitBudgetNs);   // default budget: never exit with copies in flight
       }
     }
   } else if (warp == 1) {
@@ -230,10 +231,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int local = 0;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++local) {
         // the single accumulator set must have been drained by the epilogue
-        if (!mbar_wait(accempty, (local & 1) ^ 1u)) { ok = false; break; }
+        if (!mbar_wait(accempty, (local & 1) ^ 1u, p.wait_ns)) { ok = false; break; }
         tc_fence_after();
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&tfull[t.slot], t.phase) || !mbar_wait(&bfull[b.slot], b.phase)) {
+          if (!mbar_wait(&tfull[t.slot], t.phase, p.wait_ns) || !mbar_wait(&bfull[b.slot], b.phase, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       fetch(1, nxt);
       for (int kt = 0; kt < KT; ++kt) {
         fetch(kt + 2, nnx);
-        if (!warp_wait(&bempty[br.slot], br.phase ^ 1u)) {
+        if (!warp_wait(&bempty[br.slot], br.phase ^ 1u, p.wait_ns)) {
           ok = false;
           break;
         }
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (p.tma_store && lane == 0) tma_prefetch_desc(&tm_y);
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
-      if (!warp_wait(accfull, local & 1)) break;
+      if (!warp_wait(accfull, local & 1, p.wait_ns)) break;
       tc_fence_after();
       int mt, nt;
       tile_coords(p, tile, mt, nt);
@@ -450,7 +451,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    mbar_wait(drain, 0);   // every issued MMA has finished before TMEM is released
+    mbar_wait(drain, 0, kWaitBudgetNs);   // every issued MMA has finished before TMEM is released
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -38,6 +39,8 @@ struct DeviceState {
 
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
+// Budget of every bounded wait in the kernels launched from now on (process-wide).
+std::atomic<unsigned long long> g_wait_budget_ns{kWaitBudgetNs};
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int current_device_state(DeviceState** out) {
@@ -257,6 +260,7 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.ar_ctl = ar.ctl;
   p.ar_slot = ar.slot;
   p.ar_tail = 0;
+  p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   for (int q = 0; q < decode::AR_MAX_RANKS; ++q) p.ar_peer[q] = q < ar.world ? ar.peers[q] : 0ull;
   if (ar.world > 1) {
     // enough finishing CTAs that each thread finishes AR_ELEMS_PER_THREAD output elements
@@ -369,6 +373,7 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.bn = bn;
   p.idesc = umma_idesc_f16_f32(prefill::BMH, static_cast<uint32_t>(bn));
   p.vec_store = (aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0) ? 1 : 0;
+  p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
   prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
@@ -441,6 +446,10 @@ const void* device_reachable(const void* p) {
 }  // namespace w4a16
 
 using namespace w4a16;
+
+// Zero this device's w4a16_gemm_noalloc scratch on `stream` if it has been set up
+// (defined with the scratch array below).
+static int noalloc_scratch_zero(cudaStream_t stream, bool sync);
 
 extern "C" {
 
@@ -693,7 +702,35 @@ int w4a16_check_device_errors(void* stream, uint32_t* flags_out) {
     return W4A16_ERR_LAUNCH;
   }
   if (flags_out != nullptr) *flags_out = flags;
+  if (flags != 0) {
+    // A launch abandoned on a timeout may have left tagged piece words in the
+    // allocation-free entry point's static scratch, whose callers cannot clear
+    // it themselves: zero it here (a no-op if it was never set up).
+    const int zst = noalloc_scratch_zero(s, true);
+    if (zst != W4A16_OK) return zst;
+  }
   return flags == 0 ? W4A16_OK : W4A16_ERR_TIMEOUT;
+}
+
+int w4a16_set_wait_budget_ns(int64_t ns) {
+  if (ns < 0 || (ns > 0 && ns < 1000 * 1000) || ns > 600ll * 1000 * 1000 * 1000) return W4A16_ERR_INVALID;
+  g_wait_budget_ns.store(ns == 0 ? kWaitBudgetNs : static_cast<unsigned long long>(ns),
+                         std::memory_order_relaxed);
+  return W4A16_OK;
+}
+
+int w4a16_reset_scratch(void* workspace, int64_t workspace_bytes, void* stream) {
+  if (workspace_bytes < 0 || (workspace == nullptr && workspace_bytes != 0)) return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (workspace != nullptr && workspace_bytes > 0 &&
+      cudaMemsetAsync(workspace, 0, static_cast<size_t>(workspace_bytes), s) != cudaSuccess) {
+    cudaGetLastError();
+    return W4A16_ERR_LAUNCH;
+  }
+  return noalloc_scratch_zero(s, false);
 }
 
 }  // extern "C"
@@ -755,6 +792,23 @@ int noalloc_scratch(cudaStream_t stream, void** out) {
   return W4A16_OK;
 }
 }  // namespace
+
+static int noalloc_scratch_zero(cudaStream_t stream, bool sync) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= w4a16::kMaxDevices) {
+    cudaGetLastError();
+    return W4A16_ERR_DEVICE;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoallocScratch& sc = g_noalloc[dev];
+  if (!sc.ready) return W4A16_OK;   // set-up zeroes it before its first use
+  if (cudaMemsetAsync(sc.ptr, 0, W4A16_NOALLOC_SCRATCH_BYTES, stream) != cudaSuccess ||
+      (sync && cudaStreamSynchronize(stream) != cudaSuccess)) {
+    cudaGetLastError();
+    return W4A16_ERR_LAUNCH;
+  }
+  return W4A16_OK;
+}
 
 extern "C" int w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const void* scales,
                                   const void* zeros, const void* bias, void* y, int64_t M,

@@ -39,6 +39,8 @@ SIGNATURES = {
     "w4a16_unpack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_dequantize": ([_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_check_device_errors": ([_vp, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+    "w4a16_set_wait_budget_ns": ([_c_i64], ctypes.c_int),
+    "w4a16_reset_scratch": ([_vp, _c_i64, _vp], ctypes.c_int),
     "w4a16_gemm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                             _vp], ctypes.c_int),
     "w4a16_gemm_allreduce": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
@@ -170,7 +172,21 @@ def gemm_workspace(nbytes: int, device: torch.device, stream: int) -> torch.Tens
 
 
 def reset_workspaces() -> None:
-    """Zero every cached workspace (after a kernel reported W4A16_ERR_TIMEOUT)."""
+    """Zero every cached workspace and each device's allocation-free scratch array
+    (after a kernel reported W4A16_ERR_TIMEOUT), on the stream each workspace serves;
+    then synchronise those devices."""
     with _ws_lock:
-        for ws in _ws_cache.values():
-            ws.zero_()
+        items = list(_ws_cache.items())
+    devices = set()
+    for (dev_index, stream), ws in items:
+        with torch.cuda.device(dev_index):
+            check(lib().w4a16_reset_scratch(ws.data_ptr(), ws.numel(), stream), "w4a16_reset_scratch")
+        devices.add(dev_index)
+    for dev_index in devices:
+        torch.cuda.synchronize(dev_index)
+
+
+def set_wait_budget_ns(ns: int) -> None:
+    """Time budget of every bounded wait in kernels launched from now on (0: the
+    default 4 s). Launches already queued or captured keep their budget."""
+    check(lib().w4a16_set_wait_budget_ns(int(ns)), "w4a16_set_wait_budget_ns")

@@ -15,6 +15,11 @@ the same bits as the GEMM followed by an all-gather).
 Creating a channel is collective (every rank of the group, same order, same
 arguments); so is every call. Calls on one channel must be issued on one
 stream at a time. ``close()`` is collective as well.
+
+Failure handling: a call whose C entry point refuses it, or a ``check()`` that
+finds a kernel's bounded wait expired (a peer that never wrote its words), marks
+the channel broken -- its epochs may be out of step with the peers' -- and every
+later call raises until the ranks run the collective ``reset()``.
 """
 from __future__ import annotations
 
@@ -71,17 +76,54 @@ class PeerAllReduce:
                 self._opened.append(p.value)
         self.peers = (ctypes.c_ulonglong * self.world)(*ptrs)   # host array, copied into each launch
         self.ctl = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self._nbytes = nbytes.value
+        self.broken: str | None = None
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)   # every buffer is mapped and zero before the first call
+
+    def _usable(self) -> None:
+        if self.broken is not None:
+            raise RuntimeError(f"peer channel is broken ({self.broken}); every rank must call reset()")
+
+    def _launched(self, st: int, what: str) -> None:
+        if st != _lib.W4A16_OK:
+            self.broken = f"{what} returned status {st}"
+            _lib.check(st, what)
+
+    def check(self) -> None:
+        """Synchronise this device and raise ``W4A16Error`` if any kernel's bounded
+        wait expired since the last check (the channel is then marked broken)."""
+        try:
+            _lib.check_device_errors(self.device)
+        except _lib.W4A16Error:
+            self.broken = "a bounded wait expired"
+            raise
+
+    def reset(self) -> None:
+        """Collective: zero this rank's control words and buffer after a failure,
+        so every rank starts again from epoch 0."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)   # no rank still writes into a buffer
+        with torch.cuda.device(self.device):
+            self.ctl.zero_()
+            # the peer buffer is raw memory from w4a16_p2p_alloc: zeroed like a workspace
+            _lib.check(_lib.lib().w4a16_reset_scratch(self._own, self._nbytes, _lib.stream_of(self.device)),
+                       "w4a16_reset_scratch")
+        torch.cuda.synchronize(self.device)
+        _lib.reset_workspaces()
+        dist.barrier(group=self.group)   # every buffer is zero before the next call
+        self.broken = None
 
     def gemm(self, x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
              group_size: int, bias: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
         """fp16 ``sum over ranks of x_r @ dequant(W_r)`` [+ bias] for this rank's K-slice."""
+        self._usable()
         M, K = x.shape
         N = qweight.shape[1]
         assert M <= self.max_tokens and N == self.n, "shape outside this channel"
         assert x.is_contiguous() and x.dtype == torch.float16 and x.device == self.device
         y = out if out is not None else torch.empty((M, N), device=x.device, dtype=torch.float16)
+        assert y.is_contiguous() and y.shape == (M, N) and y.dtype == torch.float16 and y.device == x.device
         dev = x.device
         stream = _lib.stream_of(dev)
         nb = _lib.gemm_workspace_bytes(M, N, K, group_size, dev)
@@ -90,7 +132,7 @@ class PeerAllReduce:
             x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), _lib.ptr(bias),
             y.data_ptr(), M, N, K, group_size, N, _lib.ptr(ws), 0 if ws is None else ws.numel(),
             self.peers, self.world, self.rank, self.ctl.data_ptr(), self.slot, stream)
-        _lib.check(st, "w4a16_gemm_allreduce")
+        self._launched(st, "w4a16_gemm_allreduce")
         return y
 
     def gemm_allgather(self, x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
@@ -98,12 +140,14 @@ class PeerAllReduce:
                        out: torch.Tensor | None = None) -> torch.Tensor:
         """fp16 ``[x @ dequant(W_0) | ... | x @ dequant(W_{p-1})]`` (each shard's bias
         added) for this rank's column shard ``W_r``: the whole output on every rank."""
+        self._usable()
         M, K = x.shape
         N = qweight.shape[1]
         assert M <= self.max_tokens and N == self.n, "shape outside this channel"
         assert x.is_contiguous() and x.dtype == torch.float16 and x.device == self.device
         y = out if out is not None else torch.empty((M, self.world * N), device=x.device, dtype=torch.float16)
-        assert y.is_contiguous() and y.shape == (M, self.world * N)
+        assert y.is_contiguous() and y.shape == (M, self.world * N) and y.dtype == torch.float16
+        assert y.device == x.device
         dev = x.device
         stream = _lib.stream_of(dev)
         nb = _lib.gemm_workspace_bytes(M, N, K, group_size, dev)
@@ -112,7 +156,7 @@ class PeerAllReduce:
             x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), _lib.ptr(bias),
             y.data_ptr(), M, N, K, group_size, self.world * N, _lib.ptr(ws), 0 if ws is None else ws.numel(),
             self.peers, self.world, self.rank, self.ctl.data_ptr(), self.slot, stream)
-        _lib.check(st, "w4a16_gemm_allgather")
+        self._launched(st, "w4a16_gemm_allgather")
         return y
 
     def close(self) -> None:

@@ -68,6 +68,24 @@ def close_peer_channels() -> None:
     _peer_channels.clear()
 
 
+def _fused_route(world: int, enabled: bool, x: Tensor, n: int) -> bool:
+    """Whether a call takes the fused GEMM + collective kernel. The decision uses only
+    facts every rank shares (world size, the layer's switch, the token count and the
+    column count), so all ranks of a collective call choose the same route; facts that
+    could differ between ranks (contiguity, alignment) are fixed up by ``_aligned``
+    instead of changing the route."""
+    from .p2p import MAX_TOKENS
+    return (world > 1 and enabled and x.is_cuda and x.dim() == 2 and x.dtype == torch.float16
+            and x.shape[0] <= MAX_TOKENS and n % 8 == 0)
+
+
+def _aligned(x: Tensor) -> Tensor:
+    """``x`` contiguous with a 16-byte-aligned base (a fresh copy when it is not)."""
+    if x.is_contiguous() and x.data_ptr() % 16 == 0:
+        return x
+    return x.clone(memory_format=torch.contiguous_format)
+
+
 def _world(group=None) -> tuple[int, int]:
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(group), dist.get_world_size(group)
@@ -155,12 +173,11 @@ class ColumnParallelW4A16Linear(nn.Module):
         return mod
 
     def forward(self, x: Tensor, gather: bool = False) -> Tensor:
-        from .p2p import MAX_TOKENS
         n = self.out_features // self.world
-        if (gather and self.world > 1 and self.fused_gather and x.is_cuda and x.dim() == 2
-                and x.shape[0] <= MAX_TOKENS and n % 8 == 0 and x.is_contiguous()):
+        if gather and _fused_route(self.world, self.fused_gather, x, n):
             ch = _peer_channel(self.group, x.device, n)
-            return ch.gemm_allgather(x, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias)
+            return ch.gemm_allgather(_aligned(x), self.qweight, self.scales, self.zeros, self.group_size,
+                                     bias=self.bias)
         y = w4a16_matmul(x, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias)
         return gather_columns(y, self.group) if gather else y
 
@@ -201,12 +218,10 @@ class RowParallelW4A16Linear(nn.Module):
 
     def forward(self, x_local: Tensor) -> Tensor:
         """``x_local`` is this rank's K-slice of the input, ``[M, K/p]``."""
-        from .p2p import MAX_TOKENS
-        if (self.world > 1 and self.fused_allreduce and x_local.is_cuda and x_local.dim() == 2
-                and x_local.shape[0] <= MAX_TOKENS and self.out_features % 8 == 0
-                and x_local.is_contiguous()):
+        if _fused_route(self.world, self.fused_allreduce, x_local, self.out_features):
             ch = _peer_channel(self.group, x_local.device, self.out_features)
-            return ch.gemm(x_local, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias)
+            return ch.gemm(_aligned(x_local), self.qweight, self.scales, self.zeros, self.group_size,
+                           bias=self.bias)
         part = w4a16_matmul_f32(x_local, self.qweight, self.scales, self.zeros, self.group_size)
         y = all_reduce_sum(part, self.group).to(torch.float16)
         return y + self.bias if self.bias is not None else y
