@@ -71,6 +71,36 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   return d;
 }
 
+// Dequantise one packed word (8 consecutive K of one column) into 8 fp16 in
+// natural K order: pairs (k0,k1) (k2,k3) (k4,k5) (k6,k7). Byte b of the word
+// holds nibbles (2b, 2b+1); PRMT copies it into bytes 0 and 2, then one LOP3
+// keeps the low nibble in the low half (as fp16 1024 + n, magic 0x6400) and
+// the high nibble of the copy in the high half (as fp16 64 + n, magic 0x5400,
+// nibble at mantissa bits 4-7). zc = (1024+z, 64+z) makes the subtraction
+// exact; one fp16 multiply by ss = (s, s) is the reference's (q - z) * s.
+__device__ __forceinline__ uint32_t dequant_byte_pair(uint32_t w, uint32_t sel, uint32_t zc,
+                                                      uint32_t ss) {
+  const uint32_t t = lop3_and_or(prmt(w, 0u, sel), 0x00F0000Fu, 0x54006400u);
+  return hmul2_u32(hsub2_u32(t, zc), ss);
+}
+
+__device__ __forceinline__ uint4 dequant_word_nat(uint32_t w, uint32_t zc, uint32_t ss) {
+  uint4 r;
+  r.x = dequant_byte_pair(w, 0x4040u, zc, ss);
+  r.y = dequant_byte_pair(w, 0x4141u, zc, ss);
+  r.z = dequant_byte_pair(w, 0x4242u, zc, ss);
+  r.w = dequant_byte_pair(w, 0x4343u, zc, ss);
+  return r;
+}
+
+// (1024 + z, 64 + z) as one half2, from the fp16 bits of z: the subtrahend of
+// dequant_word_nat.
+__device__ __forceinline__ uint32_t zero_pair_nat(uint32_t zbits) {
+  const __half zv = __ushort_as_half(static_cast<unsigned short>(zbits));
+  return static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
+         (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
+}
+
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   // Streamed once: keep it out of L1.
   uint4 v;
@@ -113,7 +143,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 
 // try_wait suspends the thread until the phase completes or the hinted time
-// (ns) passes, so a waiting warp issues almost nothing while it waits.
+// (ns) passes, so a waiting warp issues almost nothing while it waits. (Measured
+// on B200: the hint length does not change the hand-off latency of any kernel here;
+// the form without a hint, and 20 us, gave the same times.)
 constexpr uint32_t kSuspendHintNs = 1000000u;
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {

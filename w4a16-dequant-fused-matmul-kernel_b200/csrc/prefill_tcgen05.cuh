@@ -11,13 +11,13 @@
 // B twice (once per 128-row half) -- ~150 KB per step against ~90 B/clk per SM,
 // the rate a cuBLAS bf16 GEMM at 1.63 PF implies. Wider tiles amortise the x
 // tile; the packed weights bypass shared memory. Under load a TMA load takes
-// ~1.5 us to land, so the x ring is 5 steps deep. The two M=128 x N=bn
+// ~1.5 us to land, so the x ring is TSTAGES (4) steps deep. The two M=128 x N=bn
 // accumulators fill most of TMEM, so the epilogue does not overlap the next
 // tile's MMAs; 8 epilogue warps keep that drain short. bn below 224 only serves
 // to round the tile count to whole waves of CTAs.
 //
 //   warp 0       TMA producer: per step the x tile [256 x 64] fp16 (128-byte
-//                swizzle) into a 5-deep ring on a transaction-counted mbarrier.
+//                swizzle) into a 4-deep ring on a transaction-counted mbarrier.
 //   warps 2..17  dequantisers: two threads per tile column each load 4 of the
 //                column's 8 packed words of the step and its scale and zero
 //                straight from global memory (L2-resident, two steps ahead),
@@ -107,27 +107,6 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, 
   const int rem = tile - grp * per_group;
   mt = first + rem % gm;
   nt = rem / gm;
-}
-
-// Dequantise one packed word (8 consecutive K of one column) into 8 fp16 in
-// natural K order: pairs (k0,k1) (k2,k3) (k4,k5) (k6,k7). Byte b of the word
-// holds nibbles (2b, 2b+1); PRMT copies it into bytes 0 and 2, then one LOP3
-// keeps the low nibble in the low half (as fp16 1024 + n, magic 0x6400) and
-// the high nibble of the copy in the high half (as fp16 64 + n, magic 0x5400,
-// nibble at mantissa bits 4-7). zc = (1024+z, 64+z) makes the subtraction exact.
-__device__ __forceinline__ uint32_t dequant_byte_pair(uint32_t w, uint32_t sel, uint32_t zc,
-                                                      uint32_t ss) {
-  const uint32_t t = lop3_and_or(prmt(w, 0u, sel), 0x00F0000Fu, 0x54006400u);
-  return hmul2_u32(hsub2_u32(t, zc), ss);
-}
-
-__device__ __forceinline__ uint4 dequant_word_nat(uint32_t w, uint32_t zc, uint32_t ss) {
-  uint4 r;
-  r.x = dequant_byte_pair(w, 0x4040u, zc, ss);
-  r.y = dequant_byte_pair(w, 0x4141u, zc, ss);
-  r.z = dequant_byte_pair(w, 0x4242u, zc, ss);
-  r.w = dequant_byte_pair(w, 0x4343u, zc, ss);
-  return r;
 }
 
 // Lane 0 waits, the warp follows: keeps mbarrier polling off the shared-memory pipe.
@@ -307,10 +286,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (active) {
           const uint32_t ss = cur.s * 0x10001u;
-          const __half zv = __ushort_as_half(static_cast<unsigned short>(cur.z));
-          const uint32_t zc =
-              static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(1024.0f)))) |
-              (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
+          const uint32_t zc = zero_pair_nat(cur.z);
           uint8_t* brow = bring + br.slot * B_BYTES + t * 128;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {

@@ -21,13 +21,15 @@ __all__ = ["W4A16Linear"]
 
 
 class W4A16Linear(nn.Module):
-    """4-bit weight / fp16 activation linear layer.
+    """``y = x @ W + b`` where W is held as group-wise uint4 codes and x, y are fp16.
 
-    Buffers:
-        qweight : int32 [K//8, N]
-        scales  : fp16  [K//G, N]
-        zeros   : fp16  [K//G, N]
-        bias    : fp16  [N] (optional)
+    The module stores the quantised weight exactly as ``quantize_weight`` returns
+    it, so a state_dict moves between this package and the reference unchanged:
+    ``qweight`` (int32, ``in_features/8`` rows of ``out_features`` packed words),
+    ``scales`` and ``zeros`` (fp16, one row per group of ``group_size`` input
+    features) and, when the layer has one, ``bias`` (fp16, ``out_features``).
+    Inputs of any leading shape are flattened to rows for the GEMM and the
+    result is reshaped back.
     """
 
     def __init__(
@@ -58,7 +60,9 @@ class W4A16Linear(nn.Module):
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, group_size: int = 128) -> "W4A16Linear":
-        """Quantise an existing ``nn.Linear`` (weight ``[out, in]``) into a ``W4A16Linear``."""
+        """A new layer holding ``linear``'s weight quantised with this group size (torch
+        keeps ``nn.Linear.weight`` as ``[out, in]``; it is transposed to the ``[in, out]``
+        layout the GEMM reads) and its bias in fp16."""
         N, K = linear.weight.shape
         mod = cls(
             in_features=K,
@@ -74,7 +78,8 @@ class W4A16Linear(nn.Module):
         return mod
 
     def quantize_from_dense(self, W: Tensor) -> None:
-        """Quantise a dense weight ``W`` of shape ``[K, N]`` (in_features, out_features)."""
+        """Replace the stored weight by ``W`` (``[in_features, out_features]``, any float
+        dtype) quantised on the GPU with the bit-exact quantiser."""
         assert W.shape == (self.in_features, self.out_features), (
             f"expected weight [K,N]={(self.in_features, self.out_features)}, got {tuple(W.shape)}"
         )
