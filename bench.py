@@ -18,7 +18,8 @@ Extra keys carry every other configuration of the benchmark list: ``sweep``
 (M in {1,4,8,16,32} at K=8192, N=28672/p, at every N), ``gather`` (N > 1: the
 same GEMM with the full Y on every rank, through the fused GEMM + all-gather
 kernel and through GEMM + NCCL all-gather), ``mlp_stack`` (80 decoder MLP blocks,
-gate/up column-parallel, down row-parallel with its all-reduce, M=1 and M=2048),
+gate/up column-parallel with SwiGLU fused into its epilogue, down row-parallel with
+its all-reduce, M=1 and M=2048),
 ``prefill`` (N = 1: M in {512,2048,4096,8192} at K=4096, N=14336 on the tcgen05
 kernel; ``secondary`` repeats M=4096). Each has a roofline against the measured
 peaks. Before anything is timed, every rank checks its outputs (its shard, the
@@ -489,8 +490,9 @@ def measure_gather(ctx, args, sw, X_by_M):
 
 def measure_mlp(ctx, args):
     """80 decoder MLP blocks (4 distinct weight sets cycled, >= 1.4 GB per GPU at tp1),
-    gate/up column-parallel fused into one GEMM, SwiGLU, down row-parallel with its
-    all-reduce (fused over NVLink up to 32 tokens, NCCL beyond), one CUDA graph per step.
+    gate/up column-parallel fused into one GEMM with the SwiGLU in its epilogue, down
+    row-parallel with its all-reduce (fused over NVLink up to 32 tokens, NCCL beyond),
+    one CUDA graph per step.
     Block 0's activations and reduced output are checked against the oracle first."""
     torch = ctx.torch
     import w4a16
@@ -526,8 +528,7 @@ def measure_mlp(ctx, args):
         # rank's shard, then the reduced output on sampled columns given every rank's activations
         b0 = blocks[0]
         xs = x[:4]
-        gu = w4a16.w4a16_matmul(xs, b0.gate_up.qweight, b0.gate_up.scales, b0.gate_up.zeros, G)
-        h = w4a16.swiglu(gu)
+        h = w4a16.w4a16_matmul_swiglu(xs, b0.gate_up.qweight, b0.gate_up.scales, b0.gate_up.zeros, G)
         y = b0.down(h)
         import oracle
         g_ref = oracle.reference_w4a16(xs.cpu().numpy(), *(t.cpu().numpy() for t in check["g"]), G)

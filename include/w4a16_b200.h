@@ -100,6 +100,24 @@ int w4a16_swiglu(const void* gate_up, void* h, int64_t M, int64_t N, int64_t ld_
                  int64_t ld_out, void* stream);
 
 /*
+ * The gate/up projection of an MLP block fused with its SwiGLU: the GEMM's epilogue
+ * writes h[m, j] = fp16(silu(g) * u) (fp32 math on the fp16-rounded g and u, one
+ * rounding: the same values as w4a16_gemm followed by w4a16_swiglu) instead of the
+ * [M, N] gate/up output. The weight's N columns hold the gate and up projections
+ * interleaved in blocks of 16: columns 32b .. 32b+15 are gate columns 16b .. 16b+15
+ * and columns 32b+16 .. 32b+31 the matching up columns, so output column j reads
+ * weight columns 32(j/16) + j%16 and that + 16. h: fp16 [M, N/2], row pitch ldh >= N/2.
+ * N % 32 == 0; x, qweight, scales, zeros 16-byte aligned (W4A16_ERR_ALIGNMENT
+ * otherwise); the other requirements and the workspace are w4a16_gemm's. No reference
+ * counterpart: it removes the [M, N] round trip between the projections of the MLP
+ * block the benchmark configuration names.
+ */
+int w4a16_gemm_swiglu(const void* x, const int32_t* qweight, const void* scales,
+                      const void* zeros, void* h, int64_t M, int64_t N, int64_t K,
+                      int64_t group_size, int64_t ldh, void* workspace,
+                      int64_t workspace_bytes, void* stream);
+
+/*
  * dst = src, `bytes` bytes (a multiple of 16; both 16-byte aligned), as a kernel on
  * `stream` that chains with the GEMM launches around it under programmatic
  * dependent launch. No reference counterpart: it stages a step's inputs in (or its

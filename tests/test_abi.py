@@ -135,3 +135,9 @@ def test_reset_scratch_rejects_bad_arguments_without_a_device():
     lib = _lib.lib()
     assert lib.w4a16_reset_scratch(None, 16, None) == -1
     assert lib.w4a16_reset_scratch(None, -1, None) == -1
+
+
+@pytest.mark.parametrize("N,ldh", [(48, 24), (64, 31)])   # N % 32, ldh < N/2
+def test_gemm_swiglu_rejects_bad_arguments_without_a_device(N, ldh):
+    assert _lib.lib().w4a16_gemm_swiglu(None, None, None, None, None, 1, N, 128, 64, ldh, None, 0,
+                                        None) == -1

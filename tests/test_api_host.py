@@ -64,3 +64,18 @@ def test_linear_buffers_and_state_dict_layout():
     nb = W4A16Linear(256, 48, group_size=64, bias=False)
     assert nb.bias is None and "bias" not in nb.state_dict()
     assert "group_size=64" in repr(m)
+
+
+def test_interleave_gate_up_layout():
+    """Blocks of 16 columns alternate gate, up: output column j of the fused SwiGLU
+    GEMM reads fused columns 32*(j//16) + j%16 (gate) and that + 16 (up)."""
+    R, H = 3, 48
+    g = torch.arange(R * H, dtype=torch.int32).reshape(R, H)
+    u = -g - 1
+    f = w4a16.interleave_gate_up(g, u)
+    assert f.shape == (R, 2 * H) and f.is_contiguous()
+    for j in range(H):
+        cg = 32 * (j // 16) + j % 16
+        assert torch.equal(f[:, cg], g[:, j]) and torch.equal(f[:, cg + 16], u[:, j])
+    with pytest.raises(AssertionError):
+        w4a16.interleave_gate_up(g[:, :40], u[:, :40])   # not a multiple of 16

@@ -15,7 +15,8 @@ import torch.multiprocessing as mp
 import oracle
 from helpers import gpu_case, np_
 from tolerance import assert_gemm_close
-from w4a16 import quantize_weight, swiglu, w4a16_matmul_f32
+from w4a16 import (interleave_gate_up, quantize_weight, swiglu, w4a16_matmul, w4a16_matmul_f32,
+                   w4a16_matmul_swiglu)
 from w4a16.parallel import ColumnParallelW4A16Linear, RowParallelW4A16Linear, W4A16MLP
 
 pytestmark = pytest.mark.gpu
@@ -55,6 +56,29 @@ def test_swiglu_matches_fp32_reference():
     h = swiglu(gu)
     ref = _silu_mul(np_(gu[:, :136]), np_(gu[:, 136:]))
     assert np.max(np.abs(np_(h).astype(np.float32) - ref.astype(np.float32))) <= 2e-3 * (1 + np.abs(ref).max())
+
+
+@pytest.mark.parametrize("M,K,H", [(1, 1024, 208), (5, 512, 64), (9, 1024, 336), (32, 2048, 512),
+                                   (33, 512, 208), (300, 1024, 336)])
+def test_fused_swiglu_gemm_matches_gemm_then_swiglu(M, K, H):
+    """The SwiGLU epilogue (decode route up to 32 tokens, tcgen05 route beyond) gives
+    the bits of the plain GEMM on the same interleaved weights followed by the SwiGLU
+    kernel, and agrees with the oracle."""
+    G = 128 if K % 128 == 0 else 64
+    X, Wg = gpu_case(M, K, H, G, sigma=0.05, seed=M + H)
+    _, Wu = gpu_case(1, K, H, G, sigma=0.05, seed=M + H + 1)
+    qg, qu = quantize_weight(Wg, G), quantize_weight(Wu, G)
+    fused = [interleave_gate_up(a, b) for a, b in zip(qg, qu)]
+    h = w4a16_matmul_swiglu(X, *fused, G)
+    assert h.shape == (M, H) and h.dtype == torch.float16
+    gu = w4a16_matmul(X, *fused, G).view(M, H // 16, 2, 16)
+    ref = swiglu(torch.cat([gu[:, :, 0].reshape(M, H), gu[:, :, 1].reshape(M, H)], dim=1))
+    assert torch.equal(h, ref), f"max |d| {float((h.float() - ref.float()).abs().max())}"
+    g = oracle.reference_w4a16(np_(X), *(np_(t) for t in qg), G)
+    u = oracle.reference_w4a16(np_(X), *(np_(t) for t in qu), G)
+    want = _silu_mul(g, u).astype(np.float32)
+    err = np.abs(np_(h).astype(np.float32) - want)
+    assert np.all(err <= 2e-2 + 4e-3 * np.abs(want)), float(err.max())
 
 
 @pytest.mark.parametrize("M", [1, 64])

@@ -101,6 +101,15 @@ __device__ __forceinline__ uint32_t zero_pair_nat(uint32_t zbits) {
          (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
 }
 
+// SwiGLU of one output element: h = fp16(silu(g) * u) of the fp16-rounded gate and
+// up values, in fp32 with one final rounding. Every path (the separate kernel on an
+// fp16 gate/up output, and the GEMM epilogues that fuse it) uses this function.
+__device__ __forceinline__ __half swiglu_h(float g, float u) {
+  const float gh = __half2float(__float2half_rn(g));
+  const float uh = __half2float(__float2half_rn(u));
+  return __float2half_rn(gh / (1.0f + expf(-gh)) * uh);
+}
+
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   // Streamed once: keep it out of L1.
   uint4 v;

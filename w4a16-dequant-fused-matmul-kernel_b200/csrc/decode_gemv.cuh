@@ -6,7 +6,8 @@
 //
 // Design (B200):
 //  * Stream-K over units of (128-column strip, 512-K stage), strip-major,
-//    dealt in equal contiguous ranges to one CTA per SM (two per SM for up to
+//    dealt in contiguous ranges (sizes differing by at most one unit, the longer
+//    ones first) to one CTA per SM (two per SM for up to
 //    8 tokens), so every SM streams the same number of bytes whatever N and K are.
 //  * One producer thread streams each unit -- packed words [64 x 128] int32,
 //    the scale and zero rows it needs and the matching x slice -- into a
@@ -104,6 +105,10 @@ struct Params {
   long long ar_slot;                    // elements per rank slot (>= M * N)
   unsigned long long ar_peer[8];        // [ar_world] buffer addresses (kernel parameters)
   unsigned long long wait_ns;           // budget of every bounded wait (%globaltimer ns)
+  // SwiGLU epilogue (w4a16_gemm_swiglu): the weight's columns are a fused gate/up
+  // projection interleaved in blocks of 16 (16 gate columns, then the same 16 up
+  // columns), and y is h [M, N/2] = fp16(silu(fp16(g)) * fp16(u)).
+  int swiglu;
 };
 
 // Peer-to-peer all-reduce buffer (one per rank): two halves, selected by the
@@ -174,9 +179,21 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// First unit of CTA p when U units are dealt to P CTAs in contiguous ranges.
+// First unit of CTA p when U units are dealt to P CTAs in contiguous ranges: every CTA
+// gets U / P units and the first U % P CTAs one more. The lowest block indices are
+// dispatched first -- under programmatic dependent launch they take the SM slots that
+// free up first, so their weights are prefetched earliest -- and the last CTAs to
+// start, whose first loads land latest, get the shorter ranges. (Spreading the extra
+// units evenly over the indices put them on late starters too: measured on B200,
+// those CTAs set the end of every launch.)
 __device__ __forceinline__ long long unit_begin(long long p, long long U, long long P) {
-  return (p * U) / P;
+  const long long b = U / P, e = U % P;
+  return p * b + (p < e ? p : e);
+}
+// The CTA whose range holds unit u (the inverse of unit_begin).
+__device__ __forceinline__ long long unit_owner(long long u, long long U, long long P) {
+  const long long b = U / P, e = U % P;
+  return u < e * (b + 1) ? u / (b + 1) : e + (u - e * (b + 1)) / b;
 }
 
 // Consumer-warp-only barrier (named barrier 1; the producer warp does not take part).
@@ -226,6 +243,11 @@ __device__ __forceinline__ void emit(const Params& p, int t, int n, float v, int
   static_cast<__half*>(p.y)[o] = h;
 }
 
+// SwiGLU of a fused gate/up strip: output column o (0..63) of a 128-column strip
+// reads the strip's column swiglu_gate_col(o) as gate and the one 16 further as up.
+constexpr int SWIGLU_BLOCK = 16;
+__device__ __forceinline__ int swiglu_gate_col(int o) { return ((o >> 4) << 5) | (o & 15); }
+
 // AR: fused all-reduce (w4a16_gemm_allreduce); a separate instantiation so the
 // plain GEMM's register allocation is not shaped by it.
 template <int MT, bool AR>
@@ -274,7 +296,7 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     range_i[1] = static_cast<int>(a - lo);
     range_i[2] = cl;
     range_i[3] = static_cast<int>((b - 1) - static_cast<long long>(cl) * KS);
-    range_i[4] = static_cast<int>(((lo + 1) * P + U - 1) / U - 1);
+    range_i[4] = static_cast<int>(unit_owner(lo, U, P));
     for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NCW);
@@ -523,7 +545,20 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
       }
       consumer_sync<NCW>();
       const bool whole = (k == KS - 1) && static_cast<long long>(c) * KS >= u0;
-      if (whole) {
+      if (whole && p.swiglu) {
+        for (int idx = ctid; idx < M * (BN / 2); idx += NCW * 32) {
+          const int t = idx / (BN / 2), o = idx % (BN / 2);
+          const int cg = swiglu_gate_col(o);
+          float vg = 0.0f, vu = 0.0f;
+#pragma unroll
+          for (int j = 0; j < KQ; ++j) {
+            vg += red[(j * MT * 8 + t) * BN + cg];
+            vu += red[(j * MT * 8 + t) * BN + cg + SWIGLU_BLOCK];
+          }
+          const int no = c * (BN / 2) + o;
+          if (2 * no < p.N) static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + no] = swiglu_h(vg, vu);
+        }
+      } else if (whole) {
         for (int idx = ctid; idx < M * BN; idx += NCW * 32) {
           const int t = idx / BN, cc = idx % BN;
           float v = 0.0f;
@@ -604,7 +639,22 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
       }
       v += own_parked ? park[t * BN + cc] : own_final(t, cc);
       const int n = cs * BN + cc;
-      if (n < p.N) emit<AR>(p, t, n, v, ar_epoch, smem_u32(ar_peer_smem));
+      if (p.swiglu) {
+        park[t * BN + cc] = v;   // the strip's sums; paired below
+      } else if (n < p.N) {
+        emit<AR>(p, t, n, v, ar_epoch, smem_u32(ar_peer_smem));
+      }
+    }
+    if (p.swiglu) {
+      consumer_sync<NCW>();
+      for (int idx = ctid; idx < M * (BN / 2); idx += NCW * 32) {
+        const int t = idx / (BN / 2), o = idx % (BN / 2);
+        const int cg = swiglu_gate_col(o);
+        const int no = cs * (BN / 2) + o;
+        if (2 * no < p.N)
+          static_cast<__half*>(p.y)[static_cast<long long>(t) * p.ldy + no] =
+              swiglu_h(park[t * BN + cg], park[t * BN + cg + SWIGLU_BLOCK]);
+      }
     }
   }
 

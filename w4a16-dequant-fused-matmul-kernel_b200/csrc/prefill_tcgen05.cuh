@@ -91,6 +91,8 @@ struct Params {
   uint32_t idesc;  // tcgen05 instruction descriptor for M=128, N=bn
   int vec_store;   // y and ldy allow 16-byte stores
   unsigned long long wait_ns;   // budget of every bounded wait (%globaltimer ns)
+  int swiglu;      // (w4a16_tcgen05_kernel<true> only) fused gate/up columns interleaved in
+                   // blocks of 16: y = h [M, N/2]
 };
 
 // Tile order: groups of RASTER_M row tiles, column-major inside a group, so that a
@@ -126,6 +128,9 @@ struct Ring {
   }
 };
 
+// SWIGLU: the epilogue pairs each 32-column chunk's gate and up halves (see Params);
+// a separate instantiation so the plain GEMM's epilogue is unchanged.
+template <bool SWIGLU>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
                          const Params p) {
@@ -371,6 +376,31 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (lane == 0 && mrow0 < p.M && n0 + col < p.N) {
             tma_store_2d_hint(&tm_y, sb, n0 + col, mrow0, y_policy);
             bulk_commit_group();
+          }
+          continue;
+        }
+        if constexpr (SWIGLU) {
+          // 32-column chunk = 16 gate columns then the same 16 up columns (tiles start on
+          // multiples of 32): 16 outputs of this row, columns (n0 + col) / 2 onwards
+          const int no = (n0 + col) / 2;
+          if (m < p.M && 2 * no < p.N) {
+            uint32_t packed[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const __half lo = swiglu_h(__uint_as_float(r[2 * e]), __uint_as_float(r[16 + 2 * e]));
+              const __half hi = swiglu_h(__uint_as_float(r[2 * e + 1]), __uint_as_float(r[16 + 2 * e + 1]));
+              packed[e] = static_cast<uint32_t>(__half_as_ushort(lo)) |
+                          (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+            }
+            __half* hrow = static_cast<__half*>(p.y) + static_cast<long long>(m) * p.ldy + no;
+            if (p.vec_store) {
+              *reinterpret_cast<uint4*>(hrow) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+              *reinterpret_cast<uint4*>(hrow + 8) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            } else {
+              const __half* hp = reinterpret_cast<const __half*>(packed);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) hrow[e] = hp[e];
+            }
           }
           continue;
         }

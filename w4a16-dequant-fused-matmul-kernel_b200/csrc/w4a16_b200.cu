@@ -35,6 +35,9 @@ struct DeviceState {
   bool is_sm100 = false;
   bool attrs_set = false;
   int num_sms = 0;
+  // set (release) once the fields above are final for an sm_100 device: later calls
+  // read them without taking the mutex
+  std::atomic<bool> ready{false};
 };
 
 std::mutex g_mu;
@@ -48,6 +51,10 @@ int current_device_state(DeviceState** out) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     cudaGetLastError();
     return W4A16_ERR_DEVICE;
+  }
+  if (g_dev[dev].ready.load(std::memory_order_acquire)) {
+    *out = &g_dev[dev];
+    return W4A16_OK;
   }
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceState& d = g_dev[dev];
@@ -65,7 +72,10 @@ int current_device_state(DeviceState** out) {
   }
   if (!d.is_sm100) return W4A16_ERR_DEVICE;
   if (!d.attrs_set) {
-    if (cudaFuncSetAttribute(prefill::w4a16_tcgen05_kernel,
+    if (cudaFuncSetAttribute(prefill::w4a16_tcgen05_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             prefill::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(prefill::w4a16_tcgen05_kernel<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              prefill::SMEM_BYTES) != cudaSuccess) {
       cudaGetLastError();
@@ -90,6 +100,7 @@ int current_device_state(DeviceState** out) {
     }
     d.attrs_set = true;
   }
+  d.ready.store(true, std::memory_order_release);
   *out = &d;
   return W4A16_OK;
 }
@@ -222,7 +233,7 @@ struct ArArgs {
 int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                       const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                       long long ldy, void* workspace, int64_t workspace_bytes,
-                      cudaStream_t stream, const ArArgs& ar = ArArgs()) {
+                      cudaStream_t stream, const ArArgs& ar = ArArgs(), int swiglu = 0) {
   DecodePlan d;
   int st = plan_decode(dev, M, N, K, &d);
   if (st != W4A16_OK) return st;
@@ -260,6 +271,7 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.ar_ctl = ar.ctl;
   p.ar_slot = ar.slot;
   p.ar_tail = 0;
+  p.swiglu = swiglu;
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   for (int q = 0; q < decode::AR_MAX_RANKS; ++q) p.ar_peer[q] = q < ar.world ? ar.peers[q] : 0ull;
   if (ar.world > 1) {
@@ -338,7 +350,7 @@ int choose_prefill_bn(int M, int N, int num_sms) {
 
 int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                    const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
-                   long long ldy, cudaStream_t stream) {
+                   long long ldy, cudaStream_t stream, int swiglu = 0) {
   const int bn = choose_prefill_bn(M, N, dev.num_sms);
   CUtensorMap tx, ty;
   if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
@@ -349,7 +361,7 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   // boxes, fp16 rows of 64 B (64-byte swizzle) or fp32 rows of 128 B (128-byte swizzle).
   const bool y_aligned = aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0;
   const bool tma_store =
-      y_aligned && (y_f32 ? make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, N, M, ldy, 32, 32,
+      !swiglu && y_aligned && (y_f32 ? make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, N, M, ldy, 32, 32,
                                         CU_TENSOR_MAP_SWIZZLE_128B)
                           : make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y, N, M, ldy, 32, 32,
                                         CU_TENSOR_MAP_SWIZZLE_64B));
@@ -373,10 +385,14 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.bn = bn;
   p.idesc = umma_idesc_f16_f32(prefill::BMH, static_cast<uint32_t>(bn));
   p.vec_store = (aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0) ? 1 : 0;
+  p.swiglu = swiglu;
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
-  prefill::w4a16_tcgen05_kernel<<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
+  if (swiglu)
+    prefill::w4a16_tcgen05_kernel<true><<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
+  else
+    prefill::w4a16_tcgen05_kernel<false><<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
   W4A16_RETURN_IF_LAUNCH_FAILED();
   return W4A16_OK;
 }
@@ -389,9 +405,7 @@ __global__ void swiglu_kernel(const __half* __restrict__ gu, __half* __restrict_
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= M * N) return;
   const int64_t m = idx / N, n = idx % N;
-  const float g = __half2float(gu[m * ld_in + n]);
-  const float u = __half2float(gu[m * ld_in + N + n]);
-  h[m * ld_out + n] = __float2half_rn(g / (1.0f + expf(-g)) * u);
+  h[m * ld_out + n] = swiglu_h(__half2float(gu[m * ld_in + n]), __half2float(gu[m * ld_in + N + n]));
 }
 
 // dst = src in 16-byte units, as a kernel that chains with the kernels around it
@@ -554,6 +568,32 @@ int w4a16_swiglu(const void* gate_up, void* h, int64_t M, int64_t N, int64_t ld_
       static_cast<const __half*>(gate_up), static_cast<__half*>(h), M, N, ld_in, ld_out);
   W4A16_RETURN_IF_LAUNCH_FAILED();
   return W4A16_OK;
+}
+
+int w4a16_gemm_swiglu(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                      void* h, int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t ldh,
+                      void* workspace, int64_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
+  if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
+  if (N % (2 * decode::SWIGLU_BLOCK) != 0 || ldh < N / 2) return W4A16_ERR_INVALID;
+  if (M == 0 || N == 0) return W4A16_OK;
+  if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || h == nullptr)
+    return W4A16_ERR_INVALID;
+  if (N > (1ll << 30) || K > (1ll << 30) || M > (1ll << 31) - 1) return W4A16_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales) || !aligned16(zeros))
+    return W4A16_ERR_ALIGNMENT;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int n = static_cast<int>(N), k = static_cast<int>(K), g = static_cast<int>(group_size);
+  if (M <= 32 && (N + decode::BN - 1) / decode::BN <= decode::MAX_STRIPS)
+    return launch_decode_tma(*dev, static_cast<const __half*>(x), qweight, static_cast<const __half*>(scales),
+                             static_cast<const __half*>(zeros), nullptr, h, 0, static_cast<int>(M), n, k, g,
+                             ldh, workspace, workspace_bytes, s, ArArgs(), 1);
+  return launch_prefill(*dev, static_cast<const __half*>(x), qweight, static_cast<const __half*>(scales),
+                        static_cast<const __half*>(zeros), nullptr, h, 0, static_cast<int>(M), n, k, g, ldh, s,
+                        1);
 }
 
 int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* stream) {

@@ -31,6 +31,8 @@ SIGNATURES = {
     "w4a16_gemm_f32": ([_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp,
                         _c_i64, _vp], ctypes.c_int),
     "w4a16_swiglu": ([_vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
+    "w4a16_gemm_swiglu": ([_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
+                           _vp], ctypes.c_int),
     "w4a16_stage": ([_vp, _vp, _c_i64, ctypes.c_int, _vp], ctypes.c_int),
     "w4a16_gemm_workspace_size": ([_c_i64, _c_i64, _c_i64, _c_i64, ctypes.POINTER(_c_i64)],
                                   ctypes.c_int),
@@ -108,6 +110,13 @@ def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def stream_of_index(index: int) -> int:
+    """Raw cudaStream_t of torch's current stream on CUDA device ``index``."""
+    if _raw_stream is not None:
+        return _raw_stream(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -169,6 +178,31 @@ def gemm_workspace(nbytes: int, device: torch.device, stream: int) -> torch.Tens
             ws = torch.zeros(size, dtype=torch.uint8, device=device)
             _ws_cache[key] = ws
         return ws
+
+
+_ws_for: dict[tuple[int, int, int, int, int, int], tuple[int | None, int]] = {}
+
+
+def workspace_for(M: int, N: int, K: int, G: int, device_index: int, stream: int) -> tuple[int | None, int]:
+    """(pointer, bytes) of the zeroed workspace a GEMM of this shape uses on ``stream``
+    of device ``device_index``; (None, 0) when the shape needs none. Memoised: a hit
+    is one dictionary lookup (the buffer it names is kept alive by the cache below)."""
+    key = (M, N, K, G, device_index, stream)
+    hit = _ws_for.get(key)
+    if hit is not None:
+        return hit
+    dev = torch.device("cuda", device_index)
+    nbytes = gemm_workspace_bytes(M, N, K, G, dev) if M > 0 and N > 0 else 0
+    ws = gemm_workspace(nbytes, dev, stream)
+    val = (None, 0) if ws is None else (ws.data_ptr(), ws.numel())
+    with _ws_lock:
+        # a later, larger request can replace the stream's buffer: drop memoised entries
+        # that name a retired buffer
+        live = {t.data_ptr() for t in _ws_cache.values()}
+        for k in [k for k, v in _ws_for.items() if v[0] is not None and v[0] not in live]:
+            del _ws_for[k]
+        _ws_for[key] = val
+    return val
 
 
 def reset_workspaces() -> None:

@@ -28,6 +28,9 @@ __all__ = ["w4a16_matmul"]
 
 # The reference's smallest and largest BLOCK_K; every group size must be a multiple of both.
 _BLOCK_K_RULE = 64
+_F16, _I32 = torch.float16, torch.int32
+_current_device = torch._C._cuda_getDevice if hasattr(torch._C, "_cuda_getDevice") else torch.cuda.current_device
+_raw_stream = _lib.stream_of_index
 
 
 def w4a16_matmul(
@@ -55,6 +58,41 @@ def w4a16_matmul(
     Returns:
         fp16 tensor [M, N].
     """
+    # The common case in one expression (cheap tensor attributes, no temporaries);
+    # anything unusual goes through the detailed checks below, which raise the
+    # reference's AssertionError with its message.
+    xs, qs = x.shape, qweight.shape
+    d = x.get_device()
+    if not (len(xs) == 2 and len(qs) == 2 and d >= 0 and x.dtype is _F16 and qweight.dtype is _I32
+            and scales.dtype is _F16 and zeros.dtype is _F16 and qs[0] * 8 == xs[1]
+            and group_size > 0 and xs[1] % group_size == 0 and group_size % _BLOCK_K_RULE == 0
+            and scales.shape == (xs[1] // group_size, qs[1]) and zeros.shape == scales.shape
+            and qweight.get_device() == d and scales.get_device() == d and zeros.get_device() == d
+            and x.is_contiguous() and qweight.is_contiguous() and scales.is_contiguous()
+            and zeros.is_contiguous()):
+        _check_inputs(x, qweight, scales, zeros, group_size)
+    M, K = xs
+    N = qs[1]
+    if bias is not None:
+        assert bias.get_device() == d, "bias must be on the inputs' CUDA device"
+        assert bias.dtype is _F16 and bias.shape == (N,) and bias.is_contiguous(), (
+            f"bias must be a contiguous fp16 [{N}] tensor"
+        )
+
+    if out is None:
+        y = torch.empty((M, N), device=d, dtype=_F16)
+    else:
+        assert out.shape == (M, N) and out.dtype is _F16 and out.is_contiguous()
+        assert out.get_device() == d, "out must be on the inputs' CUDA device"
+        y = out
+
+    _launch(x, qweight, scales, zeros, bias, y, M, N, K, group_size, N)
+    return y
+
+
+def _check_inputs(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int) -> None:
+    """The reference's assertions (triton_kernel.py:153-182) and this library's device
+    rule, one by one, so a bad call fails with the specific message."""
     assert x.is_cuda, "x must be on CUDA (a B200 / sm_100 device)"
     assert qweight.is_cuda and scales.is_cuda and zeros.is_cuda, "all inputs must be on CUDA"
     assert x.dtype == torch.float16, f"x must be fp16, got {x.dtype}"
@@ -85,42 +123,27 @@ def w4a16_matmul(
     assert qweight.device == dev and scales.device == dev and zeros.device == dev, (
         "all inputs must be on the same CUDA device"
     )
-    if bias is not None:
-        assert bias.is_cuda and bias.device == dev, "bias must be on the inputs' CUDA device"
-        assert bias.dtype == torch.float16 and bias.shape == (N,) and bias.is_contiguous(), (
-            f"bias must be a contiguous fp16 [{N}] tensor"
-        )
-
-    if out is None:
-        y = torch.empty((M, N), device=dev, dtype=torch.float16)
-    else:
-        assert out.shape == (M, N) and out.dtype == torch.float16 and out.is_contiguous()
-        assert out.device == dev, "out must be on the inputs' CUDA device"
-        y = out
-
-    _launch(x, qweight, scales, zeros, bias, y, M, N, K, group_size, N)
-    return y
 
 
 def _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy) -> None:
-    dev = x.device
-    if dev.index != torch.cuda.current_device():
-        with torch.cuda.device(dev):
+    d = x.get_device()
+    if d != _current_device():
+        with torch.cuda.device(d):
             return _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy)
-    stream = _lib.stream_of(dev)
-    ws = _lib.gemm_workspace(_lib.gemm_workspace_bytes(M, N, K, G, dev), dev, stream) \
-        if M > 0 and N > 0 else None
-    if y.dtype == torch.float32:
+    stream = _raw_stream(d)
+    ws_ptr, ws_bytes = _lib.workspace_for(M, N, K, G, d, stream)
+    if y.dtype is torch.float32:
         assert bias is None
         st = _lib.lib().w4a16_gemm_f32(
             x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-            y.data_ptr(), M, N, K, G, ldy, _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
+            y.data_ptr(), M, N, K, G, ldy, ws_ptr, ws_bytes, stream)
     else:
         st = _lib.lib().w4a16_gemm(
             x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-            _lib.ptr(bias), y.data_ptr(), M, N, K, G, ldy,
-            _lib.ptr(ws), 0 if ws is None else ws.numel(), stream)
-    _lib.check(st, "w4a16_gemm")
+            None if bias is None else bias.data_ptr(), y.data_ptr(), M, N, K, G, ldy,
+            ws_ptr, ws_bytes, stream)
+    if st:
+        _lib.check(st, "w4a16_gemm")
 
 
 def w4a16_matmul_f32(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
@@ -152,6 +175,52 @@ def swiglu(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
         st = _lib.lib().w4a16_swiglu(gate_up.data_ptr(), out.data_ptr(), M, H, H2, H,
                                      _lib.stream_of(dev))
     _lib.check(st, "w4a16_swiglu")
+    return out
+
+
+SWIGLU_BLOCK = 16
+
+
+def interleave_gate_up(gate: Tensor, up: Tensor, block: int = SWIGLU_BLOCK) -> Tensor:
+    """``[R, H]`` gate and up column blocks side by side in blocks of ``block``
+    columns (gate block b, then up block b, ...): the ``[R, 2H]`` layout
+    :func:`w4a16_matmul_swiglu` reads. Applies to qweight, scales and zeros alike."""
+    assert gate.shape == up.shape and gate.dim() == 2 and gate.shape[1] % block == 0
+    R, H = gate.shape
+    return torch.stack([gate.reshape(R, H // block, block), up.reshape(R, H // block, block)],
+                       dim=2).reshape(R, 2 * H).contiguous()
+
+
+def w4a16_matmul_swiglu(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
+                        out: Tensor | None = None) -> Tensor:
+    """``silu(x @ W_gate) * (x @ W_up)`` in one GEMM whose epilogue applies SwiGLU.
+
+    ``qweight`` / ``scales`` / ``zeros`` hold the gate and up projections interleaved
+    by :func:`interleave_gate_up` (``[K/8, 2H]`` etc.). Returns fp16 ``[M, H]``, the
+    same values as :func:`swiglu` of the fp16 gate/up GEMM output (no extension of the
+    reference: it fuses the MLP block's activation into the projection)."""
+    w4a16_matmul(x[:0], qweight, scales, zeros, group_size)   # the GEMM's argument checks
+    M, K = x.shape
+    N = qweight.shape[1]
+    assert N % (2 * SWIGLU_BLOCK) == 0, f"fused gate/up columns N={N} must be a multiple of {2 * SWIGLU_BLOCK}"
+    assert all(t.data_ptr() % 16 == 0 for t in (x, qweight, scales, zeros)), "inputs must be 16-byte aligned"
+    if out is None:
+        out = torch.empty((M, N // 2), device=x.device, dtype=torch.float16)
+    else:
+        assert out.shape == (M, N // 2) and out.dtype == torch.float16 and out.is_contiguous()
+        assert out.device == x.device, "out must be on the inputs' CUDA device"
+    dev = x.device
+    if dev.index != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            return w4a16_matmul_swiglu(x, qweight, scales, zeros, group_size, out)
+    if M == 0:
+        return out
+    stream = _lib.stream_of(dev)
+    ws = _lib.gemm_workspace(_lib.gemm_workspace_bytes(M, N, K, group_size, dev), dev, stream)
+    st = _lib.lib().w4a16_gemm_swiglu(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+                                      out.data_ptr(), M, N, K, group_size, N // 2, _lib.ptr(ws),
+                                      0 if ws is None else ws.numel(), stream)
+    _lib.check(st, "w4a16_gemm_swiglu")
     return out
 
 

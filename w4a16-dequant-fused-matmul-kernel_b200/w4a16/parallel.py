@@ -19,8 +19,9 @@ schemes the benchmark configurations name:
   GEMM and the all-reduce run as one kernel per rank over NVLink peer memory
   (``w4a16.p2p.PeerAllReduce``); larger inputs use NCCL.
 * ``W4A16MLP``: the decoder MLP block -- gate and up projections fused into
-  one column-parallel GEMM ([gate shard | up shard] side by side), SwiGLU,
-  then the row-parallel down projection and its all-reduce.
+  one column-parallel GEMM (the shards' columns interleaved in blocks of 16)
+  whose epilogue applies SwiGLU, then the row-parallel down projection and its
+  all-reduce.
 
 Without an initialised process group (or with one rank) the layers run
 unsharded and communicate nothing.
@@ -31,7 +32,7 @@ import torch
 import torch.distributed as dist
 from torch import Tensor, nn
 
-from .gemm import swiglu, w4a16_matmul, w4a16_matmul_f32
+from .gemm import interleave_gate_up, w4a16_matmul, w4a16_matmul_f32, w4a16_matmul_swiglu
 from .quant import quantize_weight
 
 __all__ = [
@@ -239,8 +240,10 @@ class _QuantizedWeight(nn.Module):
 
 class W4A16MLP(nn.Module):
     """Decoder MLP block ``down(silu(gate(x)) * up(x))`` with W4A16 weights,
-    tensor-parallel over the process group: gate/up column-parallel (fused
-    into one GEMM), down row-parallel with an fp32 all-reduce."""
+    tensor-parallel over the process group: gate/up column-parallel, fused into
+    one GEMM whose epilogue computes the SwiGLU (``gate_up`` holds this rank's
+    gate and up shards interleaved in blocks of 16 columns), then down
+    row-parallel with its all-reduce."""
 
     def __init__(self, hidden: int, intermediate: int, group_size: int = 128, device=None,
                  group=None) -> None:
@@ -251,7 +254,8 @@ class W4A16MLP(nn.Module):
             raise ValueError(f"intermediate={intermediate} must divide over {self.world} ranks")
         h = intermediate // self.world
         self.hidden, self.intermediate, self.group_size = hidden, intermediate, group_size
-        # this rank's [gate shard | up shard] side by side: one GEMM with N = 2h
+        # this rank's gate and up shards, columns interleaved in blocks of 16: one GEMM
+        # with N = 2h whose epilogue writes silu(gate) * up
         self.gate_up = _QuantizedWeight(hidden, 2 * h, group_size, device)
         self.down = RowParallelW4A16Linear(intermediate, hidden, group_size, bias=False,
                                            device=device, group=group)
@@ -273,13 +277,13 @@ class W4A16MLP(nn.Module):
         g = shard_columns(*gate, r, p)[:3]
         u = shard_columns(*up, r, p)[:3]
         for name, a, b in zip(("qweight", "scales", "zeros"), g, u):
-            getattr(self.gate_up, name).copy_(torch.cat([a, b], dim=1))
+            getattr(self.gate_up, name).copy_(interleave_gate_up(a, b))
         d = shard_rows(*down, self.group_size, r, p)
         for name, t in zip(("qweight", "scales", "zeros"), d):
             getattr(self.down, name).copy_(t)
         return self
 
     def forward(self, x: Tensor) -> Tensor:
-        gu = w4a16_matmul(x, self.gate_up.qweight, self.gate_up.scales, self.gate_up.zeros,
-                          self.group_size)
-        return self.down(swiglu(gu))
+        h = w4a16_matmul_swiglu(x, self.gate_up.qweight, self.gate_up.scales, self.gate_up.zeros,
+                                self.group_size)
+        return self.down(h)
