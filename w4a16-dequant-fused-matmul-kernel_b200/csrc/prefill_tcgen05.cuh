@@ -52,7 +52,8 @@ namespace prefill {
 constexpr int BM = 256;                      // two 128-row MMA halves
 constexpr int BMH = 128;
 constexpr int BN_MAX = 224;                  // tile columns: runtime bn in [128, 224], bn % 32 == 0
-constexpr int BN_MIN = 128;
+constexpr int BN_MIN = 128;                  // two halves; a single-half tile (M <= 128) goes down to 64
+constexpr int BN_MIN_SINGLE = 64;
 constexpr int BK = 64;
 constexpr int TSTAGES = 4;                   // x-tile ring depth (covers ~1.5 us TMA latency under load)
 constexpr int BSTAGES = 2;                   // dequantised-B ring depth
@@ -87,6 +88,8 @@ struct Params {
   int g_shift;     // log2(G) when G is a power of two, else -1
   long long ldy;
   int m_tiles, n_tiles;
+  int halves;      // 128-row MMA halves per tile: 2 (256-row tiles), or 1 when M <= 128
+  int bm;          // tile rows, 128 * halves
   int bn;          // tile columns
   uint32_t idesc;  // tcgen05 instruction descriptor for M=128, N=bn
   int vec_store;   // y and ldy allow 16-byte stores
@@ -189,11 +192,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
         int mt, nt;
         tile_coords(p, tile, mt, nt);
-        const int m0 = mt * BM;
+        const int m0 = mt * p.bm;
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u, p.wait_ns)) { ok = false; break; }
           uint8_t* st = tring + r.slot * T_BYTES;
-          mbar_arrive_expect_tx(&tfull[r.slot], A_BYTES);
+          mbar_arrive_expect_tx(&tfull[r.slot], p.halves * (A_BYTES / 2));   // the x box is [bm x 64]
           tma_load_2d(st, &tm_x, &tfull[r.slot], kt * BK, m0);
           r.advance(TSTAGES);
           ++issued;
@@ -232,8 +235,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t acc = (kt | kk) != 0 ? 1u : 0u;
             tc_mma_f16(tmem_base, adesc0 + static_cast<uint64_t>(kk * 2),
                        bdesc + static_cast<uint64_t>(kk * 2), p.idesc, acc);
-            tc_mma_f16(tmem_base + bn, adesc1 + static_cast<uint64_t>(kk * 2),
-                       bdesc + static_cast<uint64_t>(kk * 2), p.idesc, acc);
+            if (p.halves == 2)
+              tc_mma_f16(tmem_base + bn, adesc1 + static_cast<uint64_t>(kk * 2),
+                         bdesc + static_cast<uint64_t>(kk * 2), p.idesc, acc);
           }
           tc_commit(&tempty[t.slot]);
           tc_commit(&bempty[b.slot]);
@@ -325,10 +329,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int mt, nt;
       tile_coords(p, tile, mt, nt);
       const int n0 = nt * bn;
-      const int mrow0 = mt * BM + h * BMH + quarter * 32;
+      const int mrow0 = mt * p.bm + h * BMH + quarter * 32;
       const int m = mrow0 + lane;
 #pragma unroll 1
-      for (int col = 0; col < bn; col += 32) {
+      for (int col = 0; col < (h < p.halves ? bn : 0); col += 32) {   // (a missing half has no rows)
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + h * bn + col + (static_cast<uint32_t>(quarter * 32) << 16), r);
         tmem_ld_wait();

@@ -331,14 +331,16 @@ int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, 
 // larger of its MMAs (4 * bn cycles) and its operand traffic (x tile 32 KB plus
 // a per-column share, at the ~32 B/clk per SM measured on B200). Wider tiles
 // reuse the x tile more; narrower ones can round the tile count to whole waves.
-int choose_prefill_bn(int M, int N, int num_sms) {
-  const long long m_tiles = (M + prefill::BM - 1) / prefill::BM;
+int choose_prefill_bn(int M, int N, int num_sms, int halves) {
+  const int bm = prefill::BMH * halves;
+  const long long m_tiles = (M + bm - 1) / bm;
   int best = prefill::BN_MAX;
   double best_t = 1e300;
-  for (int bn = prefill::BN_MAX; bn >= prefill::BN_MIN; bn -= 32) {
+  const int bn_min = halves == 2 ? prefill::BN_MIN : prefill::BN_MIN_SINGLE;
+  for (int bn = prefill::BN_MAX; bn >= bn_min; bn -= 32) {
     const long long tiles = m_tiles * ((N + bn - 1) / bn);
     const long long waves = (tiles + num_sms - 1) / num_sms;
-    const double step = std::max(4.0 * bn, (prefill::A_BYTES + 36.0 * bn) / 31.5);
+    const double step = std::max(2.0 * halves * bn, (prefill::A_BYTES / 2 * halves + 36.0 * bn) / 31.5);
     const double t = static_cast<double>(waves) * step;
     if (t < best_t * 0.999) {
       best_t = t;
@@ -351,10 +353,13 @@ int choose_prefill_bn(int M, int N, int num_sms) {
 int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                    const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                    long long ldy, cudaStream_t stream, int swiglu = 0) {
-  const int bn = choose_prefill_bn(M, N, dev.num_sms);
+  // up to 128 tokens one 128-row MMA half per tile: no idle MMA rows, half the x traffic,
+  // and narrower tiles (bn down to 64) so that one row of tiles spreads over the SMs
+  const int halves = M <= prefill::BMH ? 1 : 2;
+  const int bn = choose_prefill_bn(M, N, dev.num_sms, halves);
   CUtensorMap tx, ty;
-  if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK, prefill::BM,
-                   CU_TENSOR_MAP_SWIZZLE_128B)) {
+  if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill::BK,
+                   static_cast<uint32_t>(prefill::BMH * halves), CU_TENSOR_MAP_SWIZZLE_128B)) {
     return W4A16_ERR_ALIGNMENT;
   }
   // y through TMA stores when its base and row pitch are 16-byte aligned: 32 x 32
@@ -380,7 +385,9 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.G = G;
   p.g_shift = ((G & (G - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(G)) : -1;
   p.ldy = ldy;
-  p.m_tiles = (M + prefill::BM - 1) / prefill::BM;
+  p.halves = halves;
+  p.bm = prefill::BMH * halves;
+  p.m_tiles = (M + p.bm - 1) / p.bm;
   p.n_tiles = (N + bn - 1) / bn;
   p.bn = bn;
   p.idesc = umma_idesc_f16_f32(prefill::BMH, static_cast<uint32_t>(bn));
