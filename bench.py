@@ -528,7 +528,8 @@ def measure_mlp(ctx, args):
         # rank's shard, then the reduced output on sampled columns given every rank's activations
         b0 = blocks[0]
         xs = x[:4]
-        h = w4a16.w4a16_matmul_swiglu(xs, b0.gate_up.qweight, b0.gate_up.scales, b0.gate_up.zeros, G)
+        h = w4a16.w4a16_matmul_swiglu(xs, b0.gate_up.qweight, b0.gate_up.scales, b0.gate_up.zeros, G,
+                                      kernel_order=b0.gate_up_kernel_order)
         y = b0.down(h)
         import oracle
         g_ref = oracle.reference_w4a16(xs.cpu().numpy(), *(t.cpu().numpy() for t in check["g"]), G)

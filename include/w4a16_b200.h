@@ -118,6 +118,41 @@ int w4a16_gemm_swiglu(const void* x, const int32_t* qweight, const void* scales,
                       int64_t workspace_bytes, void* stream);
 
 /*
+ * Option bits of w4a16_gemm_ex.
+ *   W4A16_FLAG_KERNEL_ORDER  qweight holds the kernel nibble order written by
+ *                            w4a16_repack instead of the reference's
+ *   W4A16_FLAG_SWIGLU        the w4a16_gemm_swiglu epilogue (y is h [M, N/2])
+ *   W4A16_FLAG_F32_OUT       the w4a16_gemm_f32 output (fp32, unrounded, no bias)
+ */
+#define W4A16_FLAG_KERNEL_ORDER 1u
+#define W4A16_FLAG_SWIGLU       2u
+#define W4A16_FLAG_F32_OUT      4u
+
+/*
+ * w4a16_gemm with option bits (above): one entry point for the plain, SwiGLU and
+ * fp32-output GEMMs over either nibble order. SWIGLU excludes F32_OUT and a bias;
+ * KERNEL_ORDER and SWIGLU need N % 8 == 0 and 16-byte-aligned x, qweight, scales and
+ * zeros (W4A16_ERR_ALIGNMENT otherwise). Unknown bits: W4A16_ERR_INVALID. No
+ * reference counterpart (w4a16_gemm is the reference's operator).
+ */
+int w4a16_gemm_ex(const void* x, const int32_t* qweight, const void* scales,
+                  const void* zeros, const void* bias, void* y, int64_t M, int64_t N,
+                  int64_t K, int64_t group_size, int64_t ldy, uint32_t flags,
+                  void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Offline repack of qweight [K/8, N] between the reference's nibble order (row 8i+j in
+ * nibble j of word [i, n], w4a16-kernel/src/w4a16/quant.py:45-70) and the kernel order
+ * (rows k0, k2, k4, k6, k1, k3, k5, k7 in nibbles 0..7): to_kernel_order != 0 converts
+ * reference -> kernel, 0 converts back. Elementwise; out may equal qweight. In the
+ * kernel order the GEMMs extract a word's consecutive row pairs with one shift and four
+ * masks (W4A16_FLAG_KERNEL_ORDER). No reference counterpart: a load-time layout, the
+ * stored (state_dict) format stays the reference's.
+ */
+int w4a16_repack(const int32_t* qweight, int32_t* out, int64_t K, int64_t N,
+                 int to_kernel_order, void* stream);
+
+/*
  * dst = src, `bytes` bytes (a multiple of 16; both 16-byte aligned), as a kernel on
  * `stream` that chains with the GEMM launches around it under programmatic
  * dependent launch. No reference counterpart: it stages a step's inputs in (or its

@@ -15,6 +15,7 @@ import torch
 
 import oracle
 import synth
+import w4a16
 from helpers import gpu_case, np_, torch_reference
 from tolerance import assert_gemm_close
 from w4a16 import W4A16Linear, quantize_weight, w4a16_matmul
@@ -306,3 +307,50 @@ def test_stage_copy_then_gemm_replayed_from_a_graph():
     ref = w4a16_matmul(X, qw, s, z, 128)
     for i in range(6):
         assert torch.equal(Y[i], ref), f"step {i}"
+
+
+# ----------------------------------------------------------------------------- kernel nibble order
+def _np_repack(qw: np.ndarray) -> np.ndarray:
+    """Reference nibble j -> kernel nibble {0,4,1,5,2,6,3,7}[j], restated in numpy."""
+    w = qw.view(np.uint32)
+    out = np.zeros_like(w)
+    for j in range(8):
+        pos = (j >> 1) | ((j & 1) << 2)
+        out |= ((w >> np.uint32(4 * j)) & np.uint32(0xF)) << np.uint32(4 * pos)
+    return out.view(np.int32)
+
+
+def test_repack_layout_and_round_trip():
+    qw = torch.randint(-2**31, 2**31 - 1, (96, 264), dtype=torch.int64).to(torch.int32).cuda()
+    k = w4a16.repack_qweight(qw)
+    assert np.array_equal(np_(k), _np_repack(np_(qw)))
+    assert torch.equal(w4a16.repack_qweight(k, False), qw)
+    inplace = qw.clone()
+    w4a16.repack_qweight(inplace, True, out=inplace)
+    assert torch.equal(inplace, k)
+
+
+@pytest.mark.parametrize("M,K,N,G", [(1, 4096, 11008, 128), (7, 1024, 264, 64), (32, 2048, 512, 128),
+                                     (33, 512, 256, 128), (300, 1024, 264, 128)])
+def test_kernel_order_gemm_matches_oracle(M, K, N, G):
+    X, W = gpu_case(M, K, N, G, sigma=0.05, seed=M + 5)
+    qw, s, z = quantize_weight(W, G)
+    ref = oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G)
+    bias = torch.randn(N, device="cuda").half()
+    y = w4a16_matmul(X, w4a16.repack_qweight(qw), s, z, G, kernel_order=True)
+    assert_gemm_close(np_(y), ref, f"kernel order M={M}")
+    yb = w4a16_matmul(X, w4a16.repack_qweight(qw), s, z, G, bias=bias, kernel_order=True)
+    assert_gemm_close(np_(yb), (ref + np_(bias)).astype(np.float16), f"kernel order + bias M={M}")
+
+
+def test_linear_repack_keeps_reference_state_dict():
+    lin = torch.nn.Linear(512, 264, bias=True).cuda().half()
+    a = w4a16.W4A16Linear.from_linear(lin, group_size=128)
+    b = w4a16.W4A16Linear.from_linear(lin, group_size=128).repack_()
+    x = torch.randn(5, 512, device="cuda").half()
+    assert_gemm_close(np_(b(x)), np_(a(x)), "repacked module")
+    sa, sb = a.state_dict(), b.state_dict()
+    assert sa.keys() == sb.keys() and all(torch.equal(sa[k], sb[k]) for k in sa)
+    c = w4a16.W4A16Linear(512, 264, group_size=128, device="cuda").repack_()
+    c.load_state_dict(sa)
+    assert torch.equal(c.qweight, b.qweight) and torch.equal(c(x), b(x))

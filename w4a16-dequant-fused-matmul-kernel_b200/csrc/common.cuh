@@ -101,6 +101,27 @@ __device__ __forceinline__ uint32_t zero_pair_nat(uint32_t zbits) {
          (static_cast<uint32_t>(__half_as_ushort(__hadd(zv, __float2half_rn(64.0f)))) << 16);
 }
 
+__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Dequantise one packed word into 4 half2 pairs with one shift and four LOP3s:
+// p[j] = (nibble j, nibble j + 4) for j = 0..3 (the low half from bits 4j..4j+3, the
+// high half from bits 4j+16..4j+19). In the reference's nibble order (row 8i+j at
+// nibble j) that is (k0,k4) (k1,k5) (k2,k6) (k3,k7); in the kernel order w4a16_repack
+// writes (nibbles k0,k2,k4,k6,k1,k3,k5,k7) it is (k0,k1) (k2,k3) (k4,k5) (k6,k7).
+// za = half2(1024+z), zb = half2(64+z), ss = half2(s): (q - z) exact, one rounding at * s.
+__device__ __forceinline__ void dequant_word_perm(uint32_t w, uint32_t za, uint32_t zb, uint32_t ss,
+                                                  uint32_t (&p)[4]) {
+  const uint32_t w8 = w >> 8;
+  p[0] = hmul2_u32(hsub2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), za), ss);
+  p[1] = hmul2_u32(hsub2_u32(lop3_and_or(w, 0x00F000F0u, 0x54005400u), zb), ss);
+  p[2] = hmul2_u32(hsub2_u32(lop3_and_or(w8, 0x000F000Fu, 0x64006400u), za), ss);
+  p[3] = hmul2_u32(hsub2_u32(lop3_and_or(w8, 0x00F000F0u, 0x54005400u), zb), ss);
+}
+
 // SwiGLU of one output element: h = fp16(silu(g) * u) of the fp16-rounded gate and
 // up values, in fp32 with one final rounding. Every path (the separate kernel on an
 // fp16 gate/up output, and the GEMM epilogues that fuse it) uses this function.

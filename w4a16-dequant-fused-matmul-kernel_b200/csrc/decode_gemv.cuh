@@ -155,23 +155,6 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Dequantise one packed word into 4 half2 pairs in the K-permuted order the
-// MMA fragments use: p[0] = (k0,k4), p[1] = (k1,k5), p[2] = (k2,k6), p[3] = (k3,k7).
-// za = half2(1024+z), zb = half2(64+z), ss = half2(s).
-__device__ __forceinline__ void dequant_word_perm(uint32_t w, uint32_t za, uint32_t zb, uint32_t ss,
-                                                  uint32_t (&p)[4]) {
-  const uint32_t w8 = w >> 8;
-  p[0] = hmul2_u32(hsub2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), za), ss);
-  p[1] = hmul2_u32(hsub2_u32(lop3_and_or(w, 0x00F000F0u, 0x54005400u), zb), ss);
-  p[2] = hmul2_u32(hsub2_u32(lop3_and_or(w8, 0x000F000Fu, 0x64006400u), za), ss);
-  p[3] = hmul2_u32(hsub2_u32(lop3_and_or(w8, 0x00F000F0u, 0x54005400u), zb), ss);
-}
-
-__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
 
 // Programmatic dependent launch controls.
 __device__ __forceinline__ void pdl_launch_dependents() {
@@ -250,7 +233,9 @@ __device__ __forceinline__ int swiglu_gate_col(int o) { return ((o >> 4) << 5) |
 
 // AR: fused all-reduce (w4a16_gemm_allreduce); a separate instantiation so the
 // plain GEMM's register allocation is not shaped by it.
-template <int MT, bool AR>
+// NAT: qweight in the kernel nibble order (w4a16_repack): the dequantised pairs come
+// out in natural K order, so x is used as loaded, without the 4 PRMTs per chunk.
+template <int MT, bool AR, bool NAT = false>
 __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
     decode_gemv_tma_kernel(const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_s,
@@ -500,9 +485,13 @@ __global__ void __launch_bounds__(threads_for(MT), ctas_per_sm(MT))
             // columns are garbage that is never written out (an output column of the MMA
             // depends only on its own token column)
             const uint4 v = *reinterpret_cast<const uint4*>(xq + xoff[tt] + roff * 16);
-            // (k0..k7) -> pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7), the weight fragments' K order
-            xv[tt] = make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632),
-                                prmt(v.y, v.w, 0x5410), prmt(v.y, v.w, 0x7632));
+            if constexpr (NAT) {
+              xv[tt] = v;   // the weight fragments' pairs are (k0,k1) (k2,k3) (k4,k5) (k6,k7)
+            } else {
+              // (k0..k7) -> pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7), the weight fragments' K order
+              xv[tt] = make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632),
+                                  prmt(v.y, v.w, 0x5410), prmt(v.y, v.w, 0x7632));
+            }
           }
           uint32_t d[4][4];
           dequant_word_perm(wv.x, za[0], zb[0], ss[0], d[0]);

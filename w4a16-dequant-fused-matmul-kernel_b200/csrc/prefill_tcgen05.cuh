@@ -133,7 +133,9 @@ struct Ring {
 
 // SWIGLU: the epilogue pairs each 32-column chunk's gate and up halves (see Params);
 // a separate instantiation so the plain GEMM's epilogue is unchanged.
-template <bool SWIGLU>
+// NAT: qweight in the kernel nibble order (w4a16_repack): one shift and four LOP3s
+// extract a word's natural-order pairs, instead of four PRMTs and four LOP3s.
+template <bool SWIGLU, bool NAT>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_y,
                          const Params p) {
@@ -295,11 +297,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (active) {
           const uint32_t ss = cur.s * 0x10001u;
-          const uint32_t zc = zero_pair_nat(cur.z);
           uint8_t* brow = bring + br.slot * B_BYTES + t * 128;
+          if constexpr (NAT) {
+            const uint32_t z2 = cur.z * 0x10001u;
+            const uint32_t za = hadd2_u32(z2, 0x64006400u), zb = hadd2_u32(z2, 0x54005400u);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) = dequant_word_nat(cur.w[c], zc, ss);
+            for (int c = 0; c < 4; ++c) {
+              uint32_t q[4];
+              dequant_word_perm(cur.w[c], za, zb, ss, q);
+              *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) = make_uint4(q[0], q[1], q[2], q[3]);
+            }
+          } else {
+            const uint32_t zc = zero_pair_nat(cur.z);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              *reinterpret_cast<uint4*>(brow + (((c0 + c) ^ (t & 7)) << 4)) = dequant_word_nat(cur.w[c], zc, ss);
+            }
           }
         }
         fence_proxy_async_smem();

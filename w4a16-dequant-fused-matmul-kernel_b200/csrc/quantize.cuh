@@ -141,6 +141,32 @@ __global__ void __launch_bounds__(256) unpack_int4_kernel(const int32_t* __restr
   }
 }
 
+// Nibble order of a packed word: the reference keeps row 8i+j in nibble j; the kernel
+// order keeps rows (k0, k2, k4, k6, k1, k3, k5, k7) in nibbles 0..7, so that a mask
+// with 0x000F000F (and the same after a shift by 4 or 8 or 12) extracts consecutive
+// row pairs. Elementwise over the [K/8, N] words; `to_kernel` selects the direction.
+// In-place use (in == out) is allowed.
+__device__ __forceinline__ uint32_t repack_word(uint32_t w, bool to_kernel) {
+  // reference nibble j sits at kernel nibble pos[j] = {0, 4, 1, 5, 2, 6, 3, 7}[j]
+  uint32_t r = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int pos = (j >> 1) | ((j & 1) << 2);
+    if (to_kernel)
+      r |= ((w >> (4 * j)) & 0xFu) << (4 * pos);
+    else
+      r |= ((w >> (4 * pos)) & 0xFu) << (4 * j);
+  }
+  return r;
+}
+
+__global__ void __launch_bounds__(256) repack_kernel(const int32_t* in, int32_t* out, int64_t n_words,
+                                                     int to_kernel) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n_words) return;
+  out[i] = static_cast<int32_t>(repack_word(static_cast<uint32_t>(in[i]), to_kernel != 0));
+}
+
 // w = fp16(fp16(q - z) * s): two correctly rounded fp16 operations, the same
 // as the reference's fp16 tensor arithmetic (quant.py:177).
 __global__ void __launch_bounds__(256) dequantize_kernel(const int32_t* __restrict__ packed,

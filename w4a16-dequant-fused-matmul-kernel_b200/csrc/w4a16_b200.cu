@@ -72,12 +72,14 @@ int current_device_state(DeviceState** out) {
   }
   if (!d.is_sm100) return W4A16_ERR_DEVICE;
   if (!d.attrs_set) {
-    if (cudaFuncSetAttribute(prefill::w4a16_tcgen05_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             prefill::SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(prefill::w4a16_tcgen05_kernel<true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             prefill::SMEM_BYTES) != cudaSuccess) {
+    auto set_prefill = [](auto kern) {
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill::SMEM_BYTES) ==
+             cudaSuccess;
+    };
+    if (!set_prefill(prefill::w4a16_tcgen05_kernel<false, false>) ||
+        !set_prefill(prefill::w4a16_tcgen05_kernel<true, false>) ||
+        !set_prefill(prefill::w4a16_tcgen05_kernel<false, true>) ||
+        !set_prefill(prefill::w4a16_tcgen05_kernel<true, true>)) {
       cudaGetLastError();
       return W4A16_ERR_LAUNCH;
     }
@@ -94,7 +96,11 @@ int current_device_state(DeviceState** out) {
         !set_decode(decode::decode_gemv_tma_kernel<1, true>) ||
         !set_decode(decode::decode_gemv_tma_kernel<2, true>) ||
         !set_decode(decode::decode_gemv_tma_kernel<3, true>) ||
-        !set_decode(decode::decode_gemv_tma_kernel<4, true>)) {
+        !set_decode(decode::decode_gemv_tma_kernel<4, true>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<1, false, true>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<2, false, true>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<3, false, true>) ||
+        !set_decode(decode::decode_gemv_tma_kernel<4, false, true>)) {
       cudaGetLastError();
       return W4A16_ERR_LAUNCH;
     }
@@ -233,7 +239,7 @@ struct ArArgs {
 int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                       const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                       long long ldy, void* workspace, int64_t workspace_bytes,
-                      cudaStream_t stream, const ArArgs& ar = ArArgs(), int swiglu = 0) {
+                      cudaStream_t stream, const ArArgs& ar = ArArgs(), int swiglu = 0, int nat = 0) {
   DecodePlan d;
   int st = plan_decode(dev, M, N, K, &d);
   if (st != W4A16_OK) return st;
@@ -294,7 +300,16 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   cfg.numAttrs = 1;
   cudaError_t e;
   const bool fused = ar.world > 1;
-  switch (d.MT * 2 + (fused ? 1 : 0)) {
+  if (nat && !fused) {
+    switch (d.MT) {
+      case 1: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1, false, true>, tw, ts, tz, tx, p); break;
+      case 2: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2, false, true>, tw, ts, tz, tx, p); break;
+      case 3: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<3, false, true>, tw, ts, tz, tx, p); break;
+      default: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<4, false, true>, tw, ts, tz, tx, p); break;
+    }
+  } else if (nat) {
+    return W4A16_ERR_INVALID;   // the fused collectives read the reference nibble order
+  } else switch (d.MT * 2 + (fused ? 1 : 0)) {
     case 2: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1, false>, tw, ts, tz, tx, p); break;
     case 3: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<1, true>, tw, ts, tz, tx, p); break;
     case 4: e = cudaLaunchKernelEx(&cfg, decode::decode_gemv_tma_kernel<2, false>, tw, ts, tz, tx, p); break;
@@ -352,7 +367,7 @@ int choose_prefill_bn(int M, int N, int num_sms, int halves) {
 
 int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                    const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
-                   long long ldy, cudaStream_t stream, int swiglu = 0) {
+                   long long ldy, cudaStream_t stream, int swiglu = 0, int nat = 0) {
   // up to 128 tokens one 128-row MMA half per tile: no idle MMA rows, half the x traffic,
   // and narrower tiles (bn down to 64) so that one row of tiles spreads over the SMs
   const int halves = M <= prefill::BMH ? 1 : 2;
@@ -396,10 +411,15 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
-  if (swiglu)
-    prefill::w4a16_tcgen05_kernel<true><<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
+  const dim3 blk(prefill::THREADS);
+  if (swiglu && nat)
+    prefill::w4a16_tcgen05_kernel<true, true><<<grid, blk, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
+  else if (swiglu)
+    prefill::w4a16_tcgen05_kernel<true, false><<<grid, blk, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
+  else if (nat)
+    prefill::w4a16_tcgen05_kernel<false, true><<<grid, blk, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
   else
-    prefill::w4a16_tcgen05_kernel<false><<<grid, prefill::THREADS, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
+    prefill::w4a16_tcgen05_kernel<false, false><<<grid, blk, prefill::SMEM_BYTES, stream>>>(tx, ty, p);
   W4A16_RETURN_IF_LAUNCH_FAILED();
   return W4A16_OK;
 }
@@ -515,10 +535,16 @@ int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_siz
 static int gemm_impl(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                      const void* bias, void* y, int y_f32, int64_t M, int64_t N, int64_t K,
                      int64_t group_size, int64_t ldy, void* workspace, int64_t workspace_bytes,
-                     void* stream) {
+                     void* stream, uint32_t flags = 0) {
+  const int nat = (flags & W4A16_FLAG_KERNEL_ORDER) ? 1 : 0;
+  const int swiglu = (flags & W4A16_FLAG_SWIGLU) ? 1 : 0;
+  if ((flags & ~(W4A16_FLAG_KERNEL_ORDER | W4A16_FLAG_SWIGLU | W4A16_FLAG_F32_OUT)) != 0) return W4A16_ERR_INVALID;
+  if ((flags & W4A16_FLAG_F32_OUT) != 0) y_f32 = 1;
   if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
   if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
-  if (ldy < N) return W4A16_ERR_INVALID;
+  if (swiglu && (y_f32 || bias != nullptr || N % (2 * decode::SWIGLU_BLOCK) != 0)) return W4A16_ERR_INVALID;
+  if (y_f32 && bias != nullptr) return W4A16_ERR_INVALID;
+  if (ldy < (swiglu ? N / 2 : N)) return W4A16_ERR_INVALID;
   if (M == 0 || N == 0) return W4A16_OK;
   if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || y == nullptr)
     return W4A16_ERR_INVALID;
@@ -535,13 +561,16 @@ static int gemm_impl(const void* x, const int32_t* qweight, const void* scales, 
                       aligned16(zeros);
   const int n = static_cast<int>(N), k = static_cast<int>(K), g = static_cast<int>(group_size);
   if (!tma_ok) {
+    // the plain-load fallback reads the reference layout and writes the plain output
+    if (nat || swiglu) return W4A16_ERR_ALIGNMENT;
     return launch_decode_fallback(xh, qweight, sh, zh, bh, y, y_f32, M, n, k, g, ldy, s);
   }
   if (M <= 32 && (N + decode::BN - 1) / decode::BN <= decode::MAX_STRIPS) {
     return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g,
-                             ldy, workspace, workspace_bytes, s);
+                             ldy, workspace, workspace_bytes, s, ArArgs(), swiglu, nat);
   }
-  return launch_prefill(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s);
+  return launch_prefill(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s,
+                        swiglu, nat);
 }
 
 extern "C" {
@@ -580,27 +609,32 @@ int w4a16_swiglu(const void* gate_up, void* h, int64_t M, int64_t N, int64_t ld_
 int w4a16_gemm_swiglu(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
                       void* h, int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t ldh,
                       void* workspace, int64_t workspace_bytes, void* stream) {
-  if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
-  if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
-  if (N % (2 * decode::SWIGLU_BLOCK) != 0 || ldh < N / 2) return W4A16_ERR_INVALID;
-  if (M == 0 || N == 0) return W4A16_OK;
-  if (x == nullptr || qweight == nullptr || scales == nullptr || zeros == nullptr || h == nullptr)
-    return W4A16_ERR_INVALID;
-  if (N > (1ll << 30) || K > (1ll << 30) || M > (1ll << 31) - 1) return W4A16_ERR_INVALID;
-  if (!aligned16(x) || !aligned16(qweight) || !aligned16(scales) || !aligned16(zeros))
-    return W4A16_ERR_ALIGNMENT;
+  return gemm_impl(x, qweight, scales, zeros, nullptr, h, 0, M, N, K, group_size, ldh, workspace,
+                   workspace_bytes, stream, W4A16_FLAG_SWIGLU);
+}
+
+int w4a16_gemm_ex(const void* x, const int32_t* qweight, const void* scales, const void* zeros,
+                  const void* bias, void* y, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                  int64_t ldy, uint32_t flags, void* workspace, int64_t workspace_bytes, void* stream) {
+  return gemm_impl(x, qweight, scales, zeros, bias, y, 0, M, N, K, group_size, ldy, workspace,
+                   workspace_bytes, stream, flags);
+}
+
+int w4a16_repack(const int32_t* qweight, int32_t* out, int64_t K, int64_t N, int to_kernel_order,
+                 void* stream) {
+  if (K < 0 || N < 0 || K % 8 != 0) return W4A16_ERR_INVALID;
+  if (K == 0 || N == 0) return W4A16_OK;
+  if (qweight == nullptr || out == nullptr) return W4A16_ERR_INVALID;
   DeviceState* dev = nullptr;
   int st = current_device_state(&dev);
   if (st != W4A16_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int n = static_cast<int>(N), k = static_cast<int>(K), g = static_cast<int>(group_size);
-  if (M <= 32 && (N + decode::BN - 1) / decode::BN <= decode::MAX_STRIPS)
-    return launch_decode_tma(*dev, static_cast<const __half*>(x), qweight, static_cast<const __half*>(scales),
-                             static_cast<const __half*>(zeros), nullptr, h, 0, static_cast<int>(M), n, k, g,
-                             ldh, workspace, workspace_bytes, s, ArArgs(), 1);
-  return launch_prefill(*dev, static_cast<const __half*>(x), qweight, static_cast<const __half*>(scales),
-                        static_cast<const __half*>(zeros), nullptr, h, 0, static_cast<int>(M), n, k, g, ldh, s,
-                        1);
+  const int64_t words = K / 8 * N;
+  const int64_t blocks = (words + 255) / 256;
+  if (blocks > 0x7fffffffLL) return W4A16_ERR_INVALID;
+  repack_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      qweight, out, words, to_kernel_order ? 1 : 0);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
 }
 
 int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* stream) {

@@ -18,7 +18,7 @@ Triton fallback. Importing needs no GPU; calling needs a B200.
 from __future__ import annotations
 
 from ._lib import W4A16Error, check_device_errors
-from .gemm import (interleave_gate_up, stage_copy, swiglu, w4a16_matmul, w4a16_matmul_f32,
+from .gemm import (interleave_gate_up, repack_qweight, stage_copy, swiglu, w4a16_matmul, w4a16_matmul_f32,
                    w4a16_matmul_swiglu)
 from .linear import W4A16Linear
 from .quant import dequantize_weight, pack_int4, quantize_weight, unpack_int4
@@ -38,6 +38,7 @@ __all__ = [
     "swiglu",
     "w4a16_matmul_swiglu",
     "interleave_gate_up",
+    "repack_qweight",
     "stage_copy",
     "W4A16Error",
     "check_device_errors",

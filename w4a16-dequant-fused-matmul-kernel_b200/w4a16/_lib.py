@@ -16,6 +16,9 @@ import torch
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libw4a16_b200.so")
 
 W4A16_OK = 0
+FLAG_KERNEL_ORDER = 1
+FLAG_SWIGLU = 2
+FLAG_F32_OUT = 4
 W4A16_ERR_TIMEOUT = -5
 W4A16_ERR_WORKSPACE = -6
 DTYPE_CODES = {torch.float16: 0, torch.float32: 1, torch.bfloat16: 2}
@@ -31,6 +34,9 @@ SIGNATURES = {
     "w4a16_gemm_f32": ([_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp,
                         _c_i64, _vp], ctypes.c_int),
     "w4a16_swiglu": ([_vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
+    "w4a16_gemm_ex": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_uint32,
+                       _vp, _c_i64, _vp], ctypes.c_int),
+    "w4a16_repack": ([_vp, _vp, _c_i64, _c_i64, ctypes.c_int, _vp], ctypes.c_int),
     "w4a16_gemm_swiglu": ([_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
                            _vp], ctypes.c_int),
     "w4a16_stage": ([_vp, _vp, _c_i64, ctypes.c_int, _vp], ctypes.c_int),

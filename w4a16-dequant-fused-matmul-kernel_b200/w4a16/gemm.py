@@ -42,6 +42,7 @@ def w4a16_matmul(
     out: Tensor | None = None,
     *,
     bias: Tensor | None = None,
+    kernel_order: bool = False,
 ) -> Tensor:
     """Fused W4A16 GEMM: ``Y = X @ dequant(qweight)`` (fp32 accumulate, fp16 out).
 
@@ -54,6 +55,8 @@ def w4a16_matmul(
         out: optional preallocated fp16 [M, N] output.
         bias: optional fp16 [N] (extension): the result is ``fp16(Y) + bias``
             rounded to fp16, fused into the kernel's epilogue.
+        kernel_order: (extension) ``qweight`` holds the kernel nibble order written
+            by :func:`repack_qweight` instead of the reference's.
 
     Returns:
         fp16 tensor [M, N].
@@ -86,7 +89,8 @@ def w4a16_matmul(
         assert out.get_device() == d, "out must be on the inputs' CUDA device"
         y = out
 
-    _launch(x, qweight, scales, zeros, bias, y, M, N, K, group_size, N)
+    _launch(x, qweight, scales, zeros, bias, y, M, N, K, group_size, N,
+            _lib.FLAG_KERNEL_ORDER if kernel_order else 0)
     return y
 
 
@@ -125,13 +129,23 @@ def _check_inputs(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, gro
     )
 
 
-def _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy) -> None:
+def _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy, flags=0) -> None:
     d = x.get_device()
     if d != _current_device():
         with torch.cuda.device(d):
-            return _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy)
+            return _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy, flags)
     stream = _raw_stream(d)
     ws_ptr, ws_bytes = _lib.workspace_for(M, N, K, G, d, stream)
+    if flags:
+        if y.dtype is torch.float32:
+            flags |= _lib.FLAG_F32_OUT
+        st = _lib.lib().w4a16_gemm_ex(
+            x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+            None if bias is None else bias.data_ptr(), y.data_ptr(), M, N, K, G, ldy, flags,
+            ws_ptr, ws_bytes, stream)
+        if st:
+            _lib.check(st, "w4a16_gemm_ex")
+        return
     if y.dtype is torch.float32:
         assert bias is None
         st = _lib.lib().w4a16_gemm_f32(
@@ -147,7 +161,7 @@ def _launch(x, qweight, scales, zeros, bias, y, M, N, K, G, ldy) -> None:
 
 
 def w4a16_matmul_f32(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
-                     out: Tensor | None = None) -> Tensor:
+                     out: Tensor | None = None, *, kernel_order: bool = False) -> Tensor:
     """``X @ dequant(qweight)`` as unrounded fp32 sums (no bias): the partial
     result of a K-sharded layer, to be summed across ranks before rounding.
     Same argument checks as :func:`w4a16_matmul`."""
@@ -158,7 +172,26 @@ def w4a16_matmul_f32(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, 
         out = torch.empty((M, N), device=x.device, dtype=torch.float32)
     else:
         assert out.shape == (M, N) and out.dtype == torch.float32 and out.is_contiguous()
-    _launch(x, qweight, scales, zeros, None, out, M, N, K, group_size, N)
+    _launch(x, qweight, scales, zeros, None, out, M, N, K, group_size, N,
+            _lib.FLAG_KERNEL_ORDER if kernel_order else 0)
+    return out
+
+
+def repack_qweight(qweight: Tensor, to_kernel_order: bool = True, out: Tensor | None = None) -> Tensor:
+    """``qweight`` [K/8, N] with its nibbles moved between the reference order (row
+    8i+j in nibble j) and the kernel order (rows k0, k2, k4, k6, k1, k3, k5, k7 in
+    nibbles 0..7) that the GEMMs read with ``kernel_order=True``. ``out`` may be
+    ``qweight`` itself (in place). No reference counterpart: a load-time layout."""
+    assert qweight.is_cuda and qweight.dtype == torch.int32 and qweight.dim() == 2
+    assert qweight.is_contiguous(), "qweight must be contiguous"
+    if out is None:
+        out = torch.empty_like(qweight)
+    assert out.shape == qweight.shape and out.dtype == torch.int32 and out.is_contiguous()
+    Kp, N = qweight.shape
+    with torch.cuda.device(qweight.device):
+        st = _lib.lib().w4a16_repack(qweight.data_ptr(), out.data_ptr(), Kp * 8, N,
+                                     1 if to_kernel_order else 0, _lib.stream_of(qweight.device))
+    _lib.check(st, "w4a16_repack")
     return out
 
 
@@ -192,7 +225,7 @@ def interleave_gate_up(gate: Tensor, up: Tensor, block: int = SWIGLU_BLOCK) -> T
 
 
 def w4a16_matmul_swiglu(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
-                        out: Tensor | None = None) -> Tensor:
+                        out: Tensor | None = None, *, kernel_order: bool = False) -> Tensor:
     """``silu(x @ W_gate) * (x @ W_up)`` in one GEMM whose epilogue applies SwiGLU.
 
     ``qweight`` / ``scales`` / ``zeros`` hold the gate and up projections interleaved
@@ -217,9 +250,10 @@ def w4a16_matmul_swiglu(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tenso
         return out
     stream = _lib.stream_of(dev)
     ws = _lib.gemm_workspace(_lib.gemm_workspace_bytes(M, N, K, group_size, dev), dev, stream)
-    st = _lib.lib().w4a16_gemm_swiglu(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
-                                      out.data_ptr(), M, N, K, group_size, N // 2, _lib.ptr(ws),
-                                      0 if ws is None else ws.numel(), stream)
+    flags = _lib.FLAG_SWIGLU | (_lib.FLAG_KERNEL_ORDER if kernel_order else 0)
+    st = _lib.lib().w4a16_gemm_ex(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(), None,
+                                  out.data_ptr(), M, N, K, group_size, N // 2, flags, _lib.ptr(ws),
+                                  0 if ws is None else ws.numel(), stream)
     _lib.check(st, "w4a16_gemm_swiglu")
     return out
 

@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor, nn
 
-from .gemm import w4a16_matmul
+from .gemm import repack_qweight, w4a16_matmul
 from .quant import quantize_weight
 
 __all__ = ["W4A16Linear"]
@@ -57,6 +57,31 @@ class W4A16Linear(nn.Module):
             self.register_buffer("bias", torch.zeros(N, dtype=torch.float16, device=device))
         else:
             self.bias = None
+        # False: ``qweight`` holds the reference nibble order; True after repack_()
+        self.kernel_order = False
+
+    def repack_(self) -> "W4A16Linear":
+        """Keep ``qweight`` in the kernel nibble order from now on (an extension of
+        the reference module): the GEMM extracts each word's row pairs with one shift
+        and four masks. ``state_dict()`` still returns the reference order and
+        ``load_state_dict()`` still takes it; the conversion happens at those two points.
+        Needs a CUDA module whose columns allow the TMA kernels (out_features % 8 == 0)."""
+        if not self.kernel_order:
+            assert self.qweight.is_cuda and self.out_features % 8 == 0, (
+                "the kernel nibble order needs a CUDA module with out_features % 8 == 0")
+            repack_qweight(self.qweight, True, out=self.qweight)
+            self.kernel_order = True
+        return self
+
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        super()._save_to_state_dict(destination, prefix, keep_vars)
+        if self.kernel_order:
+            destination[prefix + "qweight"] = repack_qweight(self.qweight.detach(), False)
+
+    def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
+        super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
+        if self.kernel_order and (prefix + "qweight") in state_dict:
+            repack_qweight(self.qweight, True, out=self.qweight)
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, group_size: int = 128) -> "W4A16Linear":
@@ -85,6 +110,8 @@ class W4A16Linear(nn.Module):
         )
         qweight, scales, zeros = quantize_weight(W, self.group_size)
         self.qweight.copy_(qweight.to(self.qweight.device))
+        if self.kernel_order:
+            repack_qweight(self.qweight, True, out=self.qweight)
         self.scales.copy_(scales.to(self.scales.device))
         self.zeros.copy_(zeros.to(self.zeros.device))
 
@@ -95,7 +122,8 @@ class W4A16Linear(nn.Module):
         )
         orig_shape = x.shape
         x2d = x.reshape(-1, self.in_features).contiguous()
-        y = w4a16_matmul(x2d, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias)
+        y = w4a16_matmul(x2d, self.qweight, self.scales, self.zeros, self.group_size, bias=self.bias,
+                         kernel_order=self.kernel_order)
         return y.reshape(*orig_shape[:-1], self.out_features)
 
     def extra_repr(self) -> str:

@@ -32,7 +32,7 @@ import torch
 import torch.distributed as dist
 from torch import Tensor, nn
 
-from .gemm import interleave_gate_up, w4a16_matmul, w4a16_matmul_f32, w4a16_matmul_swiglu
+from .gemm import interleave_gate_up, repack_qweight, w4a16_matmul, w4a16_matmul_f32, w4a16_matmul_swiglu
 from .quant import quantize_weight
 
 __all__ = [
@@ -254,9 +254,10 @@ class W4A16MLP(nn.Module):
             raise ValueError(f"intermediate={intermediate} must divide over {self.world} ranks")
         h = intermediate // self.world
         self.hidden, self.intermediate, self.group_size = hidden, intermediate, group_size
-        # this rank's gate and up shards, columns interleaved in blocks of 16: one GEMM
-        # with N = 2h whose epilogue writes silu(gate) * up
+        # this rank's gate and up shards, columns interleaved in blocks of 16 and packed in
+        # the kernel nibble order: one GEMM with N = 2h whose epilogue writes silu(gate) * up
         self.gate_up = _QuantizedWeight(hidden, 2 * h, group_size, device)
+        self.gate_up_kernel_order = False
         self.down = RowParallelW4A16Linear(intermediate, hidden, group_size, bias=False,
                                            device=device, group=group)
 
@@ -278,6 +279,9 @@ class W4A16MLP(nn.Module):
         u = shard_columns(*up, r, p)[:3]
         for name, a, b in zip(("qweight", "scales", "zeros"), g, u):
             getattr(self.gate_up, name).copy_(interleave_gate_up(a, b))
+        if self.gate_up.qweight.is_cuda:
+            repack_qweight(self.gate_up.qweight, True, out=self.gate_up.qweight)
+            self.gate_up_kernel_order = True
         d = shard_rows(*down, self.group_size, r, p)
         for name, t in zip(("qweight", "scales", "zeros"), d):
             getattr(self.down, name).copy_(t)
@@ -285,5 +289,5 @@ class W4A16MLP(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         h = w4a16_matmul_swiglu(x, self.gate_up.qweight, self.gate_up.scales, self.gate_up.zeros,
-                                self.group_size)
+                                self.group_size, kernel_order=self.gate_up_kernel_order)
         return self.down(h)
