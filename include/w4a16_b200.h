@@ -123,14 +123,19 @@ int w4a16_gemm_swiglu(const void* x, const int32_t* qweight, const void* scales,
  *                            w4a16_repack instead of the reference's
  *   W4A16_FLAG_SWIGLU        the w4a16_gemm_swiglu epilogue (y is h [M, N/2])
  *   W4A16_FLAG_F32_OUT       the w4a16_gemm_f32 output (fp32, unrounded, no bias)
+ *   W4A16_FLAG_BF16_OUT      y (and bias) bf16: the fp32 sums rounded to bf16, then
+ *                            y + bias rounded again (for bf16 models, whose
+ *                            activations w4a16_convert takes to fp16 first)
  */
 #define W4A16_FLAG_KERNEL_ORDER 1u
 #define W4A16_FLAG_SWIGLU       2u
 #define W4A16_FLAG_F32_OUT      4u
+#define W4A16_FLAG_BF16_OUT     8u
 
 /*
  * w4a16_gemm with option bits (above): one entry point for the plain, SwiGLU and
- * fp32-output GEMMs over either nibble order. SWIGLU excludes F32_OUT and a bias;
+ * fp32-output GEMMs over either nibble order. SWIGLU excludes F32_OUT, BF16_OUT and a
+ * bias; F32_OUT excludes BF16_OUT and a bias;
  * KERNEL_ORDER and SWIGLU need N % 8 == 0 and 16-byte-aligned x, qweight, scales and
  * zeros (W4A16_ERR_ALIGNMENT otherwise). Unknown bits: W4A16_ERR_INVALID. No
  * reference counterpart (w4a16_gemm is the reference's operator).
@@ -139,6 +144,15 @@ int w4a16_gemm_ex(const void* x, const int32_t* qweight, const void* scales,
                   const void* zeros, const void* bias, void* y, int64_t M, int64_t N,
                   int64_t K, int64_t group_size, int64_t ldy, uint32_t flags,
                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * dst[i] = src[i] rounded to dst's type, n elements; src fp16, fp32 or bf16, dst fp16
+ * or bf16 (W4A16_DTYPE_*). For bf16 activations: bf16 -> fp16 is exact for |x| in
+ * [2^-14, 65504] (and 0), so the fp16 GEMM computes the bf16 product unchanged
+ * there. No reference counterpart (the reference takes fp16 activations only).
+ */
+int w4a16_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
+                  void* stream);
 
 /*
  * Offline repack of qweight [K/8, N] between the reference's nibble order (row 8i+j in
@@ -186,6 +200,19 @@ int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_siz
 int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales,
                    void* zeros, int64_t K, int64_t N, int64_t group_size,
                    void* stream);
+
+/*
+ * w4a16_quantize with option bits. W4A16_QUANT_SYMMETRIC: symmetric codes, the
+ * layout GPTQ-style checkpoints use with sym=True -- per (group, column) zero = 8 and
+ * scale = 2 * max|w| / 15 in fp32 (1 when not > 0), q = clamp(rint(w / scale) + 8,
+ * 0, 15) -- stored in the same qweight / scales / zeros format, so every GEMM entry
+ * point takes it unchanged. No reference counterpart (the reference quantises
+ * asymmetrically only). Unknown bits: W4A16_ERR_INVALID.
+ */
+#define W4A16_QUANT_SYMMETRIC 1u
+int w4a16_quantize_ex(const void* w, int w_dtype, int32_t* qweight, void* scales,
+                      void* zeros, int64_t K, int64_t N, int64_t group_size,
+                      uint32_t flags, void* stream);
 
 /*
  * Pack int32 codes q [K, N] (each in 0..15) into qweight [K/8, N]

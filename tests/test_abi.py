@@ -141,3 +141,7 @@ def test_reset_scratch_rejects_bad_arguments_without_a_device():
 def test_gemm_swiglu_rejects_bad_arguments_without_a_device(N, ldh):
     assert _lib.lib().w4a16_gemm_swiglu(None, None, None, None, None, 1, N, 128, 64, ldh, None, 0,
                                         None) == -1
+
+
+def test_quantize_ex_rejects_unknown_bits_without_a_device():
+    assert _lib.lib().w4a16_quantize_ex(None, 0, None, None, None, 64, 8, 64, 2, None) == -1

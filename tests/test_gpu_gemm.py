@@ -354,3 +354,28 @@ def test_linear_repack_keeps_reference_state_dict():
     c = w4a16.W4A16Linear(512, 264, group_size=128, device="cuda").repack_()
     c.load_state_dict(sa)
     assert torch.equal(c.qweight, b.qweight) and torch.equal(c(x), b(x))
+
+
+# ----------------------------------------------------------------------------- bf16 activations
+@pytest.mark.parametrize("M,K,N,G", [(1, 4096, 11008, 128), (9, 1024, 264, 64), (40, 512, 256, 128),
+                                     (300, 1024, 512, 128), (3, 256, 60, 64)])
+@pytest.mark.parametrize("kernel_order", [False, True])
+def test_bf16_activations(M, K, N, G, kernel_order):
+    if kernel_order and N % 8:
+        pytest.skip("the kernel nibble order needs the TMA route (N % 8 == 0)")
+    X, W = gpu_case(M, K, N, G, sigma=0.05, seed=M + 11)
+    xb = X.bfloat16()
+    qw, s, z = quantize_weight(W, G)
+    qk = w4a16.repack_qweight(qw) if kernel_order else qw
+    bias = torch.randn(N, device="cuda").bfloat16()
+    y = w4a16.w4a16_matmul_bf16(xb, qk, s, z, G, kernel_order=kernel_order)
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    # the same fp32 sums as the fp16 GEMM of the converted x, rounded once to bf16
+    xh = w4a16.to_fp16(xb)
+    assert torch.equal(xh.float(), xb.float())            # |x| in fp16's normal range: exact
+    f32 = w4a16.w4a16_matmul_f32(xh, qk, s, z, G, kernel_order=kernel_order)
+    assert torch.equal(y, f32.bfloat16())
+    ref = torch_reference(xh, qw, s, z, G).float()       # fp32 oracle math on the GPU
+    assert float((y.float() - ref).abs().max()) <= 1e-2 + 8e-3 * float(ref.abs().max())
+    yb = w4a16.w4a16_matmul_bf16(xb, qk, s, z, G, bias=bias, kernel_order=kernel_order)
+    assert torch.equal(yb, (y.float() + bias.float()).bfloat16())

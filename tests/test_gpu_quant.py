@@ -14,7 +14,8 @@ import torch
 import oracle
 import synth
 from helpers import bits16, np_
-from w4a16 import dequantize_weight, pack_int4, quantize_weight, unpack_int4
+from tolerance import assert_gemm_close
+from w4a16 import dequantize_weight, pack_int4, quantize_weight, unpack_int4, w4a16_matmul
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -176,3 +177,30 @@ def test_benchmark_weight_shapes_bit_exact(K, N, sigma, outliers, full):
     Wdq = dequantize_weight(qw, s, z, 128).float()
     step = s.float().repeat_interleave(128, 0)
     assert torch.all((Wdq - W.float()).abs() <= 1.05 * step + 1e-6)
+
+
+# ----------------------------------------------------------------------------- symmetric codes
+def _np_quantize_symmetric(W: np.ndarray, G: int):
+    """Symmetric group quantisation restated in numpy (fp32, IEEE division, half-even):
+    zero = 8, scale = 2 * max|w| / 15 (1 when not > 0), q = clamp(rint(w / scale) + 8, 0, 15)."""
+    K, N = W.shape
+    Wf = W.astype(np.float32).reshape(K // G, G, N)
+    amax = np.max(np.abs(Wf), axis=1)
+    scale = (np.float32(2.0) * amax) / np.float32(15.0)
+    scale = np.where(scale > 0, scale, np.float32(1.0)).astype(np.float32)
+    q = np.clip(np.rint(Wf / scale[:, None, :]) + np.float32(8.0), 0, 15).astype(np.int32).reshape(K, N)
+    return oracle.pack_int4(q), scale.astype(np.float16), np.full((K // G, N), 8.0, dtype=np.float16)
+
+
+@pytest.mark.parametrize("K,N,G", [(256, 264, 64), (1024, 512, 128), (384, 96, 192)])
+def test_symmetric_quantisation_and_gemm(K, N, G):
+    W = (torch.randn(K, N, generator=torch.Generator().manual_seed(K + N)) * 0.05).half()
+    W[:, 0] = 0.0
+    W[:G, 1] = torch.abs(W[:G, 1])   # an all-positive group
+    qw, s, z = quantize_weight(W.cuda(), G, symmetric=True)
+    eq, es, ez = _np_quantize_symmetric(W.numpy(), G)
+    assert np.array_equal(np_(qw), eq)
+    assert np.array_equal(bits16(s), bits16(es)) and np.array_equal(bits16(z), bits16(ez))
+    X = torch.randn(5, K, device="cuda").half()
+    y = w4a16_matmul(X, qw, s, z, G)
+    assert_gemm_close(np_(y), oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G), "symmetric GEMM")

@@ -122,6 +122,21 @@ __device__ __forceinline__ void dequant_word_perm(uint32_t w, uint32_t za, uint3
   p[3] = hmul2_u32(hsub2_u32(lop3_and_or(w8, 0x00F000F0u, 0x54005400u), zb), ss);
 }
 
+// The output rounding of every GEMM epilogue: fp32 v to fp16 (or bf16 when `bf16`),
+// then, with a bias of the same type, y + bias[n] rounded again (W4A16Linear's
+// separate add). Returns the 16 bits.
+__device__ __forceinline__ uint32_t out_bits(float v, const void* bias, long long n, bool bf16) {
+  if (bf16) {
+    __nv_bfloat16 h = __float2bfloat16_rn(v);
+    if (bias != nullptr)
+      h = __float2bfloat16_rn(__bfloat162float(h) + __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[n]));
+    return __bfloat16_as_ushort(h);
+  }
+  __half h = __float2half_rn(v);
+  if (bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(static_cast<const __half*>(bias)[n]));
+  return __half_as_ushort(h);
+}
+
 // SwiGLU of one output element: h = fp16(silu(g) * u) of the fp16-rounded gate and
 // up values, in fp32 with one final rounding. Every path (the separate kernel on an
 // fp16 gate/up output, and the GEMM epilogues that fuse it) uses this function.

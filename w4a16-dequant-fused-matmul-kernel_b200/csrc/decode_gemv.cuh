@@ -84,8 +84,9 @@ static_assert(W_BYTES % 128 == 0 && SZ_BYTES % 128 == 0 && (XBOX * 2) % 128 == 0
 
 struct Params {
   const __half* bias;
-  void* y;                // fp16, or fp32 when y_f32 (unrounded partial sums, no bias)
+  void* y;                // fp16, or fp32 when y_f32 (unrounded partial sums, no bias), or bf16 when y_bf16
   int y_f32;
+  int y_bf16;             // y (and bias) bf16
   unsigned long long* pieces;   // [gridDim.x][MT*8][BN] tagged piece words, zero between launches
   int M, N, K, G;
   int g_shift;            // log2(G) when G is a power of two, else -1
@@ -221,9 +222,7 @@ __device__ __forceinline__ void emit(const Params& p, int t, int n, float v, int
     static_cast<float*>(p.y)[o] = v;
     return;
   }
-  __half h = __float2half_rn(v);
-  if (p.bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(p.bias[n]));
-  static_cast<__half*>(p.y)[o] = h;
+  static_cast<unsigned short*>(p.y)[o] = static_cast<unsigned short>(out_bits(v, p.bias, n, p.y_bf16));
 }
 
 // SwiGLU of a fused gate/up strip: output column o (0..63) of a 128-column strip
@@ -778,7 +777,7 @@ __global__ void __launch_bounds__(FB_THREADS)
                                 const __half* __restrict__ scales,
                                 const __half* __restrict__ zeros, const __half* __restrict__ bias,
                                 void* __restrict__ y, int y_f32, int M, int N, int K, int G,
-                                long long ldy) {
+                                long long ldy, int y_bf16) {
   __shared__ __half xs[32][FB_KCHUNK];
   const int n = blockIdx.x * FB_THREADS + threadIdx.x;
   float acc[32];
@@ -820,9 +819,7 @@ __global__ void __launch_bounds__(FB_THREADS)
         if (y_f32) {
           static_cast<float*>(y)[o] = acc[m];
         } else {
-          __half h = __float2half_rn(acc[m]);
-          if (bias != nullptr) h = __float2half_rn(__half2float(h) + __half2float(bias[n]));
-          static_cast<__half*>(y)[o] = h;
+          static_cast<unsigned short*>(y)[o] = static_cast<unsigned short>(out_bits(acc[m], bias, n, y_bf16 != 0));
         }
       }
     }

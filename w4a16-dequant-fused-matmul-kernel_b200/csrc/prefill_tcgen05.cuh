@@ -82,8 +82,9 @@ struct Params {
   const __half* scales;    // [K/G, N]
   const __half* zeros;     // [K/G, N]
   const __half* bias;
-  void* y;         // fp16, or fp32 when y_f32 (unrounded partial sums, no bias)
+  void* y;         // fp16, or fp32 when y_f32 (unrounded partial sums, no bias), or bf16 when y_bf16
   int y_f32;
+  int y_bf16;      // y (and bias) bf16
   int M, N, K, G;
   int g_shift;     // log2(G) when G is a power of two, else -1
   long long ldy;
@@ -370,17 +371,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t packed[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              __half lo = __float2half_rn(__uint_as_float(r[2 * e]));
-              __half hi = __float2half_rn(__uint_as_float(r[2 * e + 1]));
-              if (p.bias != nullptr) {
-                const int nb = n0 + col + 2 * e;
-                const float blo = nb < p.N ? __half2float(p.bias[nb]) : 0.0f;
-                const float bhi = nb + 1 < p.N ? __half2float(p.bias[nb + 1]) : 0.0f;
-                lo = __float2half_rn(__half2float(lo) + blo);
-                hi = __float2half_rn(__half2float(hi) + bhi);
-              }
-              packed[e] = static_cast<uint32_t>(__half_as_ushort(lo)) |
-                          (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+              // (columns past N are clipped by the store; their bias is not read)
+              const int nb = n0 + col + 2 * e;
+              packed[e] = out_bits(__uint_as_float(r[2 * e]), nb < p.N ? p.bias : nullptr, nb, p.y_bf16) |
+                          (out_bits(__uint_as_float(r[2 * e + 1]), nb + 1 < p.N ? p.bias : nullptr, nb + 1,
+                                    p.y_bf16) << 16);
             }
             // 64-byte rows, 64-byte swizzle: 16-byte chunk c at c ^ ((row >> 1) & 3)
 #pragma unroll
@@ -444,14 +439,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t packed[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              __half lo = __float2half_rn(__uint_as_float(r[v * 8 + 2 * e]));
-              __half hi = __float2half_rn(__uint_as_float(r[v * 8 + 2 * e + 1]));
-              if (p.bias != nullptr) {
-                lo = __float2half_rn(__half2float(lo) + __half2float(p.bias[nb + 2 * e]));
-                hi = __float2half_rn(__half2float(hi) + __half2float(p.bias[nb + 2 * e + 1]));
-              }
-              packed[e] = static_cast<uint32_t>(__half_as_ushort(lo)) |
-                          (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+              packed[e] = out_bits(__uint_as_float(r[v * 8 + 2 * e]), p.bias, nb + 2 * e, p.y_bf16) |
+                          (out_bits(__uint_as_float(r[v * 8 + 2 * e + 1]), p.bias, nb + 2 * e + 1, p.y_bf16)
+                           << 16);
             }
             if (p.vec_store) {
               *reinterpret_cast<uint4*>(yrow + v * 8) =

@@ -32,6 +32,26 @@ __device__ __forceinline__ float clamp_0_15(float x) {
   return (x > 15.0f) ? 15.0f : x;
 }
 
+// A group's fp32 scale and zero-point from its min and max.
+// Asymmetric (the reference, quant.py:125-136): scale = (max - min) / 15 (1 when not
+// > 0), zero = clamp(rint(-min / scale), 0, 15).
+// Symmetric (the code layout GPTQ-style checkpoints use for sym=True; no counterpart
+// in the reference): scale = 2 * max(|min|, |max|) / 15 (1 when not > 0), zero = 8.
+// Codes are clamp(rint(w / scale) + zero, 0, 15) either way, in the same format.
+__device__ __forceinline__ void group_scale_zero(float mx, float mn, bool symmetric, float& scale,
+                                                 float& zero) {
+  if (symmetric) {
+    const float amax = fmaxf(fabsf(mx), fabsf(mn));
+    scale = __fdiv_rn(__fmul_rn(2.0f, amax), 15.0f);
+    scale = (scale > 0.0f) ? scale : 1.0f;
+    zero = 8.0f;
+  } else {
+    scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    scale = (scale > 0.0f) ? scale : 1.0f;
+    zero = clamp_0_15(rintf(__fdiv_rn(-mn, scale)));
+  }
+}
+
 // One thread per (group g, column n): fp32 min/max over the G rows of the
 // group, then scale / zero, then the group's codes packed 8 rows per word.
 // Bit-exact with quant.py:101-144 (IEEE division, round-half-even rintf).
@@ -40,7 +60,7 @@ __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict_
                                                             int32_t* __restrict__ qweight,
                                                             __half* __restrict__ scales,
                                                             __half* __restrict__ zeros,
-                                                            int64_t N, int64_t G) {
+                                                            int64_t N, int64_t G, int symmetric) {
   const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t g = blockIdx.y;
   if (n >= N) return;
@@ -53,9 +73,8 @@ __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict_
     mx = (v > mx) ? v : mx;
     mn = (v < mn) ? v : mn;
   }
-  float scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-  scale = (scale > 0.0f) ? scale : 1.0f;
-  const float zero = clamp_0_15(rintf(__fdiv_rn(-mn, scale)));
+  float scale, zero;
+  group_scale_zero(mx, mn, symmetric != 0, scale, zero);
 
   scales[g * N + n] = __float2half_rn(scale);
   zeros[g * N + n] = __float2half_rn(zero);
@@ -85,7 +104,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) pack_ragged_groups_kernel(const T* __restrict__ w,
                                                                  int32_t* __restrict__ qweight,
                                                                  int64_t N, int64_t K,
-                                                                 int64_t G) {
+                                                                 int64_t G, int symmetric) {
   const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t i = blockIdx.y;  // packed row
   if (n >= N) return;
@@ -104,9 +123,7 @@ __global__ void __launch_bounds__(256) pack_ragged_groups_kernel(const T* __rest
         mx = (v > mx) ? v : mx;
         mn = (v < mn) ? v : mn;
       }
-      scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-      scale = (scale > 0.0f) ? scale : 1.0f;
-      zero = clamp_0_15(rintf(__fdiv_rn(-mn, scale)));
+      group_scale_zero(mx, mn, symmetric != 0, scale, zero);
     }
     const float v = load_as_f32(w + k * N + n);
     const float q = clamp_0_15(__fadd_rn(rintf(__fdiv_rn(v, scale)), zero));

@@ -239,7 +239,8 @@ struct ArArgs {
 int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                       const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
                       long long ldy, void* workspace, int64_t workspace_bytes,
-                      cudaStream_t stream, const ArArgs& ar = ArArgs(), int swiglu = 0, int nat = 0) {
+                      cudaStream_t stream, const ArArgs& ar = ArArgs(), int swiglu = 0, int nat = 0,
+                      int y_bf16 = 0) {
   DecodePlan d;
   int st = plan_decode(dev, M, N, K, &d);
   if (st != W4A16_OK) return st;
@@ -278,6 +279,7 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
   p.ar_slot = ar.slot;
   p.ar_tail = 0;
   p.swiglu = swiglu;
+  p.y_bf16 = y_bf16;
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   for (int q = 0; q < decode::AR_MAX_RANKS; ++q) p.ar_peer[q] = q < ar.world ? ar.peers[q] : 0ull;
   if (ar.world > 1) {
@@ -328,14 +330,14 @@ int launch_decode_tma(DeviceState& dev, const __half* x, const int32_t* qw, cons
 
 int launch_decode_fallback(const __half* x, const int32_t* qw, const __half* s, const __half* z,
                            const __half* bias, void* y, int y_f32, int64_t M, int N, int K, int G,
-                           long long ldy, cudaStream_t stream) {
+                           long long ldy, cudaStream_t stream, int y_bf16 = 0) {
   for (int64_t m0 = 0; m0 < M; m0 += 32) {
     const int mc = static_cast<int>(M - m0 < 32 ? M - m0 : 32);
     decode::decode_gemv_fallback_kernel<<<grid_2d((N + decode::FB_THREADS - 1) / decode::FB_THREADS, 1),
                                           decode::FB_THREADS, 0, stream>>>(
         x + m0 * K, qw, s, z, bias,
         static_cast<uint8_t*>(y) + m0 * ldy * (y_f32 ? sizeof(float) : sizeof(__half)), y_f32, mc,
-        N, K, G, ldy);
+        N, K, G, ldy, y_bf16);
     W4A16_RETURN_IF_LAUNCH_FAILED();
   }
   return W4A16_OK;
@@ -367,7 +369,7 @@ int choose_prefill_bn(int M, int N, int num_sms, int halves) {
 
 int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                    const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
-                   long long ldy, cudaStream_t stream, int swiglu = 0, int nat = 0) {
+                   long long ldy, cudaStream_t stream, int swiglu = 0, int nat = 0, int y_bf16 = 0) {
   // up to 128 tokens one 128-row MMA half per tile: no idle MMA rows, half the x traffic,
   // and narrower tiles (bn down to 64) so that one row of tiles spreads over the SMs
   const int halves = M <= prefill::BMH ? 1 : 2;
@@ -383,8 +385,8 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   const bool tma_store =
       !swiglu && y_aligned && (y_f32 ? make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, N, M, ldy, 32, 32,
                                         CU_TENSOR_MAP_SWIZZLE_128B)
-                          : make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y, N, M, ldy, 32, 32,
-                                        CU_TENSOR_MAP_SWIZZLE_64B));
+                          : make_map_2d(&ty, y_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                        2, y, N, M, ldy, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
   if (!tma_store) ty = tx;   // unused by the kernel
   prefill::Params p;
   p.tma_store = tma_store ? 1 : 0;
@@ -408,6 +410,7 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.idesc = umma_idesc_f16_f32(prefill::BMH, static_cast<uint32_t>(bn));
   p.vec_store = (aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0) ? 1 : 0;
   p.swiglu = swiglu;
+  p.y_bf16 = y_bf16;
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
@@ -433,6 +436,21 @@ __global__ void swiglu_kernel(const __half* __restrict__ gu, __half* __restrict_
   if (idx >= M * N) return;
   const int64_t m = idx / N, n = idx % N;
   h[m * ld_out + n] = swiglu_h(__half2float(gu[m * ld_in + n]), __half2float(gu[m * ld_in + N + n]));
+}
+
+// dst[i] = round(src[i]) between fp16 / bf16 / fp32 (to fp16 or bf16): activations of a
+// bf16 model are taken to fp16 this way before the GEMM (exact for |x| in [2^-14, 65504]).
+__global__ void __launch_bounds__(256) convert_kernel(const void* src, int src_dtype, void* dst, int dst_dtype,
+                                                      int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = src_dtype == W4A16_DTYPE_F16 ? __half2float(static_cast<const __half*>(src)[i])
+                  : src_dtype == W4A16_DTYPE_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i])
+                                                  : static_cast<const float*>(src)[i];
+  if (dst_dtype == W4A16_DTYPE_BF16)
+    static_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<__half*>(dst)[i] = __float2half_rn(v);
 }
 
 // dst = src in 16-byte units, as a kernel that chains with the kernels around it
@@ -538,8 +556,11 @@ static int gemm_impl(const void* x, const int32_t* qweight, const void* scales, 
                      void* stream, uint32_t flags = 0) {
   const int nat = (flags & W4A16_FLAG_KERNEL_ORDER) ? 1 : 0;
   const int swiglu = (flags & W4A16_FLAG_SWIGLU) ? 1 : 0;
-  if ((flags & ~(W4A16_FLAG_KERNEL_ORDER | W4A16_FLAG_SWIGLU | W4A16_FLAG_F32_OUT)) != 0) return W4A16_ERR_INVALID;
+  const int y_bf16 = (flags & W4A16_FLAG_BF16_OUT) ? 1 : 0;
+  if ((flags & ~(W4A16_FLAG_KERNEL_ORDER | W4A16_FLAG_SWIGLU | W4A16_FLAG_F32_OUT | W4A16_FLAG_BF16_OUT)) != 0)
+    return W4A16_ERR_INVALID;
   if ((flags & W4A16_FLAG_F32_OUT) != 0) y_f32 = 1;
+  if (y_bf16 && (y_f32 || swiglu)) return W4A16_ERR_INVALID;
   if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
   if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
   if (swiglu && (y_f32 || bias != nullptr || N % (2 * decode::SWIGLU_BLOCK) != 0)) return W4A16_ERR_INVALID;
@@ -563,14 +584,14 @@ static int gemm_impl(const void* x, const int32_t* qweight, const void* scales, 
   if (!tma_ok) {
     // the plain-load fallback reads the reference layout and writes the plain output
     if (nat || swiglu) return W4A16_ERR_ALIGNMENT;
-    return launch_decode_fallback(xh, qweight, sh, zh, bh, y, y_f32, M, n, k, g, ldy, s);
+    return launch_decode_fallback(xh, qweight, sh, zh, bh, y, y_f32, M, n, k, g, ldy, s, y_bf16);
   }
   if (M <= 32 && (N + decode::BN - 1) / decode::BN <= decode::MAX_STRIPS) {
     return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g,
-                             ldy, workspace, workspace_bytes, s, ArArgs(), swiglu, nat);
+                             ldy, workspace, workspace_bytes, s, ArArgs(), swiglu, nat, y_bf16);
   }
   return launch_prefill(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s,
-                        swiglu, nat);
+                        swiglu, nat, y_bf16);
 }
 
 extern "C" {
@@ -618,6 +639,23 @@ int w4a16_gemm_ex(const void* x, const int32_t* qweight, const void* scales, con
                   int64_t ldy, uint32_t flags, void* workspace, int64_t workspace_bytes, void* stream) {
   return gemm_impl(x, qweight, scales, zeros, bias, y, 0, M, N, K, group_size, ldy, workspace,
                    workspace_bytes, stream, flags);
+}
+
+int w4a16_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, void* stream) {
+  if (n < 0) return W4A16_ERR_INVALID;
+  if (n == 0) return W4A16_OK;
+  if (src == nullptr || dst == nullptr) return W4A16_ERR_INVALID;
+  if (src_dtype < W4A16_DTYPE_F16 || src_dtype > W4A16_DTYPE_BF16) return W4A16_ERR_INVALID;
+  if (dst_dtype != W4A16_DTYPE_F16 && dst_dtype != W4A16_DTYPE_BF16) return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  const int64_t blocks = (n + 255) / 256;
+  if (blocks > 0x7fffffffLL) return W4A16_ERR_INVALID;
+  convert_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      src, src_dtype, dst, dst_dtype, n);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
 }
 
 int w4a16_repack(const int32_t* qweight, int32_t* out, int64_t K, int64_t N, int to_kernel_order,
@@ -670,8 +708,8 @@ int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* 
   return W4A16_OK;
 }
 
-int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,
-                   int64_t K, int64_t N, int64_t group_size, void* stream) {
+static int quantize_impl(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,
+                         int64_t K, int64_t N, int64_t group_size, int symmetric, void* stream) {
   if (K < 0 || N < 0 || group_size <= 0) return W4A16_ERR_INVALID;
   if (K % 8 != 0 || K % group_size != 0) return W4A16_ERR_INVALID;
   if (K == 0 || N == 0) return W4A16_OK;
@@ -688,15 +726,15 @@ int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales, v
   switch (w_dtype) {
     case W4A16_DTYPE_F16:
       quantize_pack_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(w), qweight, sh,
-                                                         zh, N, group_size);
+                                                         zh, N, group_size, symmetric);
       break;
     case W4A16_DTYPE_F32:
       quantize_pack_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(w), qweight, sh,
-                                                        zh, N, group_size);
+                                                        zh, N, group_size, symmetric);
       break;
     case W4A16_DTYPE_BF16:
       quantize_pack_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(w), qweight, sh, zh, N, group_size);
+          static_cast<const __nv_bfloat16*>(w), qweight, sh, zh, N, group_size, symmetric);
       break;
     default:
       return W4A16_ERR_INVALID;
@@ -707,20 +745,32 @@ int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales, v
     switch (w_dtype) {
       case W4A16_DTYPE_F16:
         pack_ragged_groups_kernel<__half><<<pg, 256, 0, s>>>(static_cast<const __half*>(w), qweight,
-                                                              N, K, group_size);
+                                                              N, K, group_size, symmetric);
         break;
       case W4A16_DTYPE_F32:
         pack_ragged_groups_kernel<float><<<pg, 256, 0, s>>>(static_cast<const float*>(w), qweight,
-                                                             N, K, group_size);
+                                                             N, K, group_size, symmetric);
         break;
       default:
         pack_ragged_groups_kernel<__nv_bfloat16><<<pg, 256, 0, s>>>(
-            static_cast<const __nv_bfloat16*>(w), qweight, N, K, group_size);
+            static_cast<const __nv_bfloat16*>(w), qweight, N, K, group_size, symmetric);
         break;
     }
     W4A16_RETURN_IF_LAUNCH_FAILED();
   }
   return W4A16_OK;
+}
+
+int w4a16_quantize(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,
+                   int64_t K, int64_t N, int64_t group_size, void* stream) {
+  return quantize_impl(w, w_dtype, qweight, scales, zeros, K, N, group_size, 0, stream);
+}
+
+int w4a16_quantize_ex(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,
+                      int64_t K, int64_t N, int64_t group_size, uint32_t flags, void* stream) {
+  if ((flags & ~W4A16_QUANT_SYMMETRIC) != 0) return W4A16_ERR_INVALID;
+  return quantize_impl(w, w_dtype, qweight, scales, zeros, K, N, group_size,
+                       (flags & W4A16_QUANT_SYMMETRIC) ? 1 : 0, stream);
 }
 
 int w4a16_pack_int4(const int32_t* q, int32_t* qweight, int64_t K, int64_t N, void* stream) {

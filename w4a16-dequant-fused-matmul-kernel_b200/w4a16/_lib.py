@@ -19,6 +19,7 @@ W4A16_OK = 0
 FLAG_KERNEL_ORDER = 1
 FLAG_SWIGLU = 2
 FLAG_F32_OUT = 4
+FLAG_BF16_OUT = 8
 W4A16_ERR_TIMEOUT = -5
 W4A16_ERR_WORKSPACE = -6
 DTYPE_CODES = {torch.float16: 0, torch.float32: 1, torch.bfloat16: 2}
@@ -37,12 +38,15 @@ SIGNATURES = {
     "w4a16_gemm_ex": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_uint32,
                        _vp, _c_i64, _vp], ctypes.c_int),
     "w4a16_repack": ([_vp, _vp, _c_i64, _c_i64, ctypes.c_int, _vp], ctypes.c_int),
+    "w4a16_convert": ([_vp, ctypes.c_int, _vp, ctypes.c_int, _c_i64, _vp], ctypes.c_int),
     "w4a16_gemm_swiglu": ([_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
                            _vp], ctypes.c_int),
     "w4a16_stage": ([_vp, _vp, _c_i64, ctypes.c_int, _vp], ctypes.c_int),
     "w4a16_gemm_workspace_size": ([_c_i64, _c_i64, _c_i64, _c_i64, ctypes.POINTER(_c_i64)],
                                   ctypes.c_int),
     "w4a16_quantize": ([_vp, ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
+    "w4a16_quantize_ex": ([_vp, ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, ctypes.c_uint32, _vp],
+                          ctypes.c_int),
     "w4a16_pack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_unpack_int4": ([_vp, _vp, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_dequantize": ([_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),

@@ -177,6 +177,49 @@ def w4a16_matmul_f32(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, 
     return out
 
 
+def to_fp16(x: Tensor, out: Tensor | None = None) -> Tensor:
+    """``x`` (bf16, fp32 or fp16, on CUDA) rounded to fp16 by the library's conversion
+    kernel. bf16 -> fp16 is exact for |x| in [2^-14, 65504] (and 0)."""
+    assert x.is_cuda and x.dtype in _lib.DTYPE_CODES and x.is_contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    assert out.shape == x.shape and out.dtype == torch.float16 and out.is_contiguous()
+    with torch.cuda.device(x.device):
+        st = _lib.lib().w4a16_convert(x.data_ptr(), _lib.DTYPE_CODES[x.dtype], out.data_ptr(),
+                                      _lib.DTYPE_CODES[torch.float16], x.numel(), _lib.stream_of(x.device))
+    _lib.check(st, "w4a16_convert")
+    return out
+
+
+def w4a16_matmul_bf16(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
+                      out: Tensor | None = None, *, bias: Tensor | None = None,
+                      kernel_order: bool = False) -> Tensor:
+    """The fused GEMM for bf16 activations (an extension: the reference takes fp16 only).
+
+    ``x`` bf16 [M, K] is converted to fp16 by the library (exact for |x| in fp16's
+    normal range, which holds for activations), the same fp16 GEMM runs, and its
+    epilogue rounds the fp32 sums to bf16 (then adds the optional bf16 ``bias``,
+    rounded again). Returns bf16 [M, N]. Weights are the usual fp16-scaled format."""
+    assert x.is_cuda and x.dtype == torch.bfloat16, f"x must be bf16 on CUDA, got {x.dtype}"
+    assert x.dim() == 2 and x.is_contiguous(), "x must be a contiguous 2D tensor"
+    xh = to_fp16(x)
+    w4a16_matmul(xh[:0], qweight, scales, zeros, group_size)   # the GEMM's argument checks
+    M, K = x.shape
+    N = qweight.shape[1]
+    d = x.get_device()
+    if bias is not None:
+        assert bias.get_device() == d and bias.dtype == torch.bfloat16 and bias.shape == (N,) and \
+            bias.is_contiguous(), f"bias must be a contiguous bf16 [{N}] tensor on the inputs' device"
+    if out is None:
+        out = torch.empty((M, N), device=d, dtype=torch.bfloat16)
+    else:
+        assert out.shape == (M, N) and out.dtype == torch.bfloat16 and out.is_contiguous()
+        assert out.get_device() == d, "out must be on the inputs' CUDA device"
+    _launch(xh, qweight, scales, zeros, bias, out, M, N, K, group_size, N,
+            _lib.FLAG_BF16_OUT | (_lib.FLAG_KERNEL_ORDER if kernel_order else 0))
+    return out
+
+
 def repack_qweight(qweight: Tensor, to_kernel_order: bool = True, out: Tensor | None = None) -> Tensor:
     """``qweight`` [K/8, N] with its nibbles moved between the reference order (row
     8i+j in nibble j) and the kernel order (rows k0, k2, k4, k6, k1, k3, k5, k7 in

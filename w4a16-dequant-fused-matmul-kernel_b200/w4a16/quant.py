@@ -78,12 +78,15 @@ def unpack_int4(qweight: Tensor, K: int | None = None) -> Tensor:
     return out.to(qweight.device)
 
 
-def quantize_weight(W: Tensor, group_size: int = 128) -> tuple[Tensor, Tensor, Tensor]:
+def quantize_weight(W: Tensor, group_size: int = 128, *, symmetric: bool = False) -> tuple[Tensor, Tensor, Tensor]:
     """Group-wise asymmetric 4-bit quantisation of ``W`` along K (bit-exact with the reference).
 
     Args:
         W: weight tensor [K, N] (fp16, bf16 or fp32; other dtypes go through fp32).
         group_size: G, number of K-rows per quantisation group. Requires G | K, 8 | K.
+        symmetric: (extension) symmetric codes as GPTQ-style checkpoints store them
+            with sym=True: zero-point 8 and scale 2 * max|w| / 15 per group, in the
+            same format (every GEMM takes it unchanged). The reference has no such mode.
 
     Returns:
         (qweight int32 [K//8, N], scales fp16 [K//G, N], zeros fp16 [K//G, N]),
@@ -112,9 +115,14 @@ def quantize_weight(W: Tensor, group_size: int = 128) -> tuple[Tensor, Tensor, T
     scales = torch.empty((K // G, N), dtype=torch.float16, device=dev)
     zeros = torch.empty((K // G, N), dtype=torch.float16, device=dev)
     with torch.cuda.device(dev):
-        st = _lib.lib().w4a16_quantize(
-            Wd.data_ptr(), _lib.DTYPE_CODES[Wd.dtype], qweight.data_ptr(), scales.data_ptr(),
-            zeros.data_ptr(), K, N, G, _lib.stream_of(dev))
+        if symmetric:
+            st = _lib.lib().w4a16_quantize_ex(
+                Wd.data_ptr(), _lib.DTYPE_CODES[Wd.dtype], qweight.data_ptr(), scales.data_ptr(),
+                zeros.data_ptr(), K, N, G, 1, _lib.stream_of(dev))
+        else:
+            st = _lib.lib().w4a16_quantize(
+                Wd.data_ptr(), _lib.DTYPE_CODES[Wd.dtype], qweight.data_ptr(), scales.data_ptr(),
+                zeros.data_ptr(), K, N, G, _lib.stream_of(dev))
     _lib.check(st, "w4a16_quantize")
     return qweight.to(W.device), scales.to(W.device), zeros.to(W.device)
 
