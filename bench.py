@@ -761,6 +761,22 @@ def run_ours(args):
     value = world * rank_bytes * args.steps / (t_ms / 1e3) / 1e9
     assert _lib.check_device_errors(dev) == 0
 
+    # the same GEMM on weights repacked once into the kernel nibble order (w4a16.repack_qweight,
+    # W4A16Linear.repack_()): a load-time layout, reported beside the drop-in headline
+    kcopies = [(w4a16.repack_qweight(q), s_, z_) for (q, s_, z_) in hw.copies]
+    yk = torch.empty_like(y)
+    w4a16.w4a16_matmul(X, *kcopies[0], G, out=yk, kernel_order=True)
+    good, _ = oracle_check(ctx, "headline (kernel nibble order)", yk[:, hw.cols_own - hw.lo], X, *hw.sample_own, G)
+    all_ok &= good
+
+    def kstep(i):
+        w4a16.w4a16_matmul(X, *kcopies[i % hw.R], G, out=yk, kernel_order=True)
+    tk = ctx.time_graph(kstep, args.steps) / 1e3 / args.steps
+    kernel_order_line = {"us_per_call": tk * 1e6, "value": world * rank_bytes / tk / 1e9, "unit": "GB/s",
+                         "roofline": hbm_roofline(rank_bytes, tk, ctx.pk, "decode_gemv_tma_kernel<1, false, true>"),
+                         "what": "the headline GEMM with qweight repacked once into the kernel nibble order"}
+    del kcopies, yk
+
     t_pipe, t_eager = measure_e2e(ctx, args, X, hw.copies, hw.R, G, n)
     e2e_value = world * rank_bytes * args.steps / (t_pipe / 1e3) / 1e9
     e2e_eager = world * rank_bytes * args.steps / (t_eager / 1e3) / 1e9
@@ -828,6 +844,7 @@ def run_ours(args):
                           "path": "the same three calls per step from Python on one stream"}},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
+        "kernel_order": kernel_order_line,
     }
     line.update(extra)
     if rank == 0 and world == 1 and not args.no_cpu:
