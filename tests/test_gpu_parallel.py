@@ -230,12 +230,14 @@ def _fused_row_rank(rank: int, world: int, port: int, q) -> None:
         q.put((rank, None, None, None, traceback.format_exc()))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpu_fused_row_parallel_gemm_allreduce():
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_gpu_fused_row_parallel_gemm_allreduce(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_row_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_fused_row_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
@@ -247,11 +249,16 @@ def test_two_gpu_fused_row_parallel_gemm_allreduce():
         assert graph_ok, f"rank {rank}: graph replays differ from the eager fused call"
         for (M, use_bias), (outs, ref) in results.items():
             for i in range(outs.shape[0]):
-                # same partials, same fp32 sum (two terms commute), one fp16 rounding
-                assert np.array_equal(outs[i], ref), f"rank {rank} M={M} bias={use_bias} call {i}"
-    # the ranks agree with each other
+                if world == 2:
+                    # same partials, same fp32 sum (two terms commute), one fp16 rounding
+                    assert np.array_equal(outs[i], ref), f"rank {rank} M={M} bias={use_bias} call {i}"
+                else:
+                    # rank-order sum vs NCCL's reduction order: equal up to fp32 reassociation
+                    assert_gemm_close(outs[i], ref, f"rank {rank} M={M} bias={use_bias} call {i}")
+    # the ranks agree with each other (every rank sums the same words in rank order)
     for key in res[0][1]:
-        assert np.array_equal(res[0][1][key][0], res[1][1][key][0])
+        for r in range(1, world):
+            assert np.array_equal(res[0][1][key][0], res[r][1][key][0])
     # and with the oracle of the unsharded layer (rebuilt here from the same seeds)
     K, N, G = 2048, 1024, 128
     for (M, use_bias), (outs, _) in res[0][1].items():
@@ -311,7 +318,9 @@ def _fused_col_rank(rank: int, world: int, port: int, q) -> None:
         for _ in range(3):
             yg = col(X, gather=True)
             yr = row(xl)
-            mixed_ok &= bool(torch.equal(yr, row_ref(xl)))
+            yr_ref = row_ref(xl)
+            mixed_ok &= bool(torch.equal(yr, yr_ref)) if world == 2 else \
+                bool(((yr.float() - yr_ref.float()).abs() <= 1e-2 + 1e-3 * yr_ref.float().abs()).all())
             mixed_ok &= bool(torch.equal(yg[:, rank * (N // world):(rank + 1) * (N // world)], col(X)))
         # the fused gather inside a CUDA graph, replayed
         eager = col(X, gather=True)
@@ -338,12 +347,14 @@ def _fused_col_rank(rank: int, world: int, port: int, q) -> None:
         q.put((rank, None, None, None, traceback.format_exc()))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpu_fused_column_parallel_gemm_allgather():
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_gpu_fused_column_parallel_gemm_allgather(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_col_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_fused_col_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
@@ -358,7 +369,8 @@ def test_two_gpu_fused_column_parallel_gemm_allgather():
                 # every column is one rank's fp16 GEMM result: the same bits as NCCL's gather
                 assert np.array_equal(outs[i], ref), f"rank {rank} M={M} bias={use_bias} call {i}"
     for key in res[0][1]:
-        assert np.array_equal(res[0][1][key][0], res[1][1][key][0])
+        for r in range(1, world):
+            assert np.array_equal(res[0][1][key][0], res[r][1][key][0])
     # and with the oracle of the unsharded layer (rebuilt here from the same seeds)
     K, N, G = 2048, 1024, 128
     for (M, use_bias), (outs, _) in res[0][1].items():
