@@ -260,6 +260,21 @@ int w4a16_check_device_errors(void* stream, uint32_t* flags_out);
 int w4a16_set_wait_budget_ns(int64_t ns);
 
 /*
+ * Prefill kernel (M > 32 tokens) selection, process-wide, for the launches after
+ * this call. W4A16_PREFILL_AUTO (the default) picks per shape between the kernel
+ * whose dequantised weights are the shared-memory B operand of tcgen05.mma
+ * (W4A16_PREFILL_SMEM_B) and the one whose dequantised weights are the
+ * tensor-memory A operand (W4A16_PREFILL_TMEM_A), by a cost model measured on
+ * B200. Forcing one exists for tests and tuning; both give results within the
+ * GEMM tolerance of each other (the same fp16 weights, fp32 sums in another order).
+ * Anything else returns W4A16_ERR_INVALID. No reference counterpart.
+ */
+#define W4A16_PREFILL_AUTO 0
+#define W4A16_PREFILL_SMEM_B 1
+#define W4A16_PREFILL_TMEM_A 2
+int w4a16_set_prefill_kernel(int which);
+
+/*
  * After W4A16_ERR_TIMEOUT: zero `workspace_bytes` of a caller's GEMM workspace
  * (when `workspace` is not NULL) and this device's w4a16_gemm_noalloc scratch
  * array (when set up), asynchronously on `stream`; allocates nothing. The next

@@ -1,0 +1,125 @@
+"""Both prefill kernels (M > 32), each forced through w4a16_set_prefill_kernel:
+the one whose dequantised weights are the shared-memory B operand of tcgen05.mma
+and the one whose dequantised weights are the tensor-memory A operand. Each must
+meet the GEMM tolerance against the oracle on its own, for every output form
+(fp16 + bias, fp32 partials, bf16, fused SwiGLU, kernel nibble order, row pitch
+without TMA stores), and the two must agree with each other.
+
+Tolerance (tests/tolerance.py): |out - ref| <= 1e-2 + 1e-3*|ref| elementwise.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import w4a16
+from helpers import gpu_case, np_, torch_reference
+from tolerance import assert_gemm_close
+from w4a16 import _lib, quantize_weight, w4a16_matmul
+
+pytestmark = pytest.mark.gpu
+KERNELS = {"smem_b": _lib.PREFILL_SMEM_B, "tmem_a": _lib.PREFILL_TMEM_A}
+
+
+@pytest.fixture(params=sorted(KERNELS))
+def kernel(request):
+    _lib.set_prefill_kernel(KERNELS[request.param])
+    try:
+        yield request.param
+    finally:
+        _lib.set_prefill_kernel(_lib.PREFILL_AUTO)
+
+
+def _build(M, K, N, G, sigma=1.0, seed=0):
+    X, W = gpu_case(M, K, N, G, sigma=sigma, seed=seed)
+    qw, s, z = quantize_weight(W, G)
+    return X, qw, s, z
+
+
+@pytest.mark.parametrize("M", [33, 64, 129, 200, 300, 777])
+@pytest.mark.parametrize("K,N,G", [(64, 8, 64), (320, 264, 64), (1024, 520, 128), (768, 256, 256), (2048, 1000, 128)])
+def test_prefill_kernel_matches_oracle(kernel, M, K, N, G):
+    X, qw, s, z = _build(M, K, N, G, seed=M * 13 + N)
+    y = w4a16_matmul(X, qw, s, z, G)
+    assert _lib.check_device_errors() == 0
+    assert_gemm_close(np_(y), oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G), f"{kernel} M={M} N={N}")
+
+
+@pytest.mark.parametrize("M", [100, 512])
+def test_prefill_kernel_output_forms(kernel, M):
+    """fp16 + bias (rounded as W4A16Linear's separate add), fp32 partials (the sums
+    the fp16 output rounds), bf16 output of bf16 activations."""
+    K, N, G = 1024, 776, 128
+    X, qw, s, z = _build(M, K, N, G, sigma=0.05, seed=M)
+    bias = (torch.randn(N, device="cuda") * 0.5).half()
+    y = w4a16_matmul(X, qw, s, z, G)
+    f32 = w4a16.w4a16_matmul_f32(X, qw, s, z, G)
+    assert torch.equal(y, f32.half())
+    yb = w4a16_matmul(X, qw, s, z, G, bias=bias)
+    assert torch.equal(yb, (y.float() + bias.float()).half())
+    xb = X.bfloat16()
+    yh = w4a16.w4a16_matmul_bf16(xb, qw, s, z, G)
+    assert torch.equal(yh, w4a16.w4a16_matmul_f32(w4a16.to_fp16(xb), qw, s, z, G).bfloat16())
+    assert_gemm_close(np_(y), np_(torch_reference(X, qw, s, z, G)), f"{kernel} forms")
+
+
+@pytest.mark.parametrize("M", [64, 300])
+def test_prefill_kernel_order_and_swiglu(kernel, M):
+    """Kernel nibble order gives the same bits as the reference order through the same
+    kernel; the fused SwiGLU epilogue gives the same bits as the GEMM followed by the
+    SwiGLU kernel."""
+    K, H, G = 1024, 512, 128
+    X, qw, s, z = _build(M, K, 2 * H, G, sigma=0.05, seed=M + 5)
+    qk = w4a16.repack_qweight(qw)
+    y = w4a16_matmul(X, qw, s, z, G)
+    assert torch.equal(w4a16_matmul(X, qk, s, z, G, kernel_order=True), y)
+    h = w4a16.w4a16_matmul_swiglu(X, qw, s, z, G)
+    v = y.view(M, H // 16, 2, 16)
+    plain = torch.cat([v[:, :, 0, :].reshape(M, H), v[:, :, 1, :].reshape(M, H)], dim=1).contiguous()
+    assert torch.equal(h, w4a16.swiglu(plain))
+    assert torch.equal(w4a16.w4a16_matmul_swiglu(X, qk, s, z, G, kernel_order=True), h)
+
+
+@pytest.mark.parametrize("pad", [0, 3])
+def test_prefill_kernel_row_pitch(kernel, pad):
+    """Two column shards written into one wider buffer (pad 3: no TMA stores); nothing
+    lands outside the shards."""
+    from w4a16.gemm import w4a16_matmul_into
+    M, K, N, G = 200, 1024, 264, 128
+    X, qw, s, z = _build(M, K, 2 * N, G, sigma=0.05, seed=3)
+    full = w4a16_matmul(X, qw, s, z, G)
+    ldy = 2 * N + pad
+    buf = torch.full((M, ldy), 7.0, device="cuda", dtype=torch.float16)
+    for r in range(2):
+        sl = slice(r * N, (r + 1) * N)
+        w4a16_matmul_into(X, qw[:, sl].contiguous(), s[:, sl].contiguous(), z[:, sl].contiguous(), G,
+                          buf[:, sl], ldy)
+    torch.cuda.synchronize()
+    assert_gemm_close(np_(buf[:, :2 * N]), np_(full).astype(np.float32), f"{kernel} row pitch")
+    if pad:
+        assert torch.all(buf[:, 2 * N:] == 7.0)
+
+
+def test_prefill_kernels_agree_at_size():
+    """The two kernels on one large shape (both within the tolerance of the torch fp32
+    reference of the oracle math, and of each other)."""
+    X, qw, s, z = _build(1536, 4096, 4096, 128, sigma=0.02, seed=9)
+    out = {}
+    try:
+        for name, which in KERNELS.items():
+            _lib.set_prefill_kernel(which)
+            out[name] = w4a16_matmul(X, qw, s, z, 128)
+    finally:
+        _lib.set_prefill_kernel(_lib.PREFILL_AUTO)
+    ref = np_(torch_reference(X, qw, s, z, 128))
+    for name, y in out.items():
+        assert_gemm_close(np_(y), ref, name)
+    assert_gemm_close(np_(out["tmem_a"]), np_(out["smem_b"]).astype(np.float32), "kernels agree")
+    assert _lib.check_device_errors() == 0
+
+
+def test_prefill_kernel_selection_rejects_unknown():
+    with pytest.raises(RuntimeError):
+        _lib.set_prefill_kernel(7)

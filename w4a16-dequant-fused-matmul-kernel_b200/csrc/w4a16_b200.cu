@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "decode_gemv.cuh"
 #include "prefill_tcgen05.cuh"
+#include "prefill_ts.cuh"
 #include "quantize.cuh"
 
 namespace w4a16 {
@@ -80,6 +81,15 @@ int current_device_state(DeviceState** out) {
         !set_prefill(prefill::w4a16_tcgen05_kernel<true, false>) ||
         !set_prefill(prefill::w4a16_tcgen05_kernel<false, true>) ||
         !set_prefill(prefill::w4a16_tcgen05_kernel<true, true>)) {
+      cudaGetLastError();
+      return W4A16_ERR_LAUNCH;
+    }
+    auto set_ts = [](auto kern) {
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_ts::SMEM_BYTES) ==
+             cudaSuccess;
+    };
+    if (!set_ts(prefill_ts::w4a16_ts_kernel<false, false>) || !set_ts(prefill_ts::w4a16_ts_kernel<false, true>) ||
+        !set_ts(prefill_ts::w4a16_ts_kernel<true, false>) || !set_ts(prefill_ts::w4a16_ts_kernel<true, true>)) {
       cudaGetLastError();
       return W4A16_ERR_LAUNCH;
     }
@@ -427,6 +437,105 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   return W4A16_OK;
 }
 
+// Which prefill kernel (and, for the TMEM-operand one, how many tokens per tile) a
+// shape gets: the smaller of waves x K steps x step time, with the step times measured
+// on B200 (M=8192, K=4096, N=14336 and the MLP block's shapes; L2 flushed):
+//   shared-memory operand kernel, 256 x 224 tile: ~1.12 us per 64-K step, nearly flat
+//     in bn (the x tile's shared-memory traffic dominates; the relative model of
+//     choose_prefill_bn scales it);
+//   TMEM-operand kernel, 256 weight columns x mt tokens: ~0.82 us at mt = 192, ~0.7 of
+//     it independent of mt.
+// The TMEM-operand tile does ~1.17x the work per unit time, so it wins unless its
+// coarser wave quantisation loses more (M = 512; N = 8192 at M = 2048). Up to 128
+// tokens the single-half shared-memory tile is kept (it spreads one row of tiles).
+// w4a16_set_prefill_kernel() overrides the choice (tests exercise both kernels).
+std::atomic<int> g_prefill_kernel{W4A16_PREFILL_AUTO};
+
+double ss_step_model(int bn, int halves) {
+  return std::max(2.0 * halves * bn, (prefill::A_BYTES / 2 * halves + 36.0 * bn) / 31.5);
+}
+
+int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt) {
+  const int force = g_prefill_kernel.load(std::memory_order_relaxed);
+  const double kt = K / static_cast<double>(prefill::BK);
+  auto waves = [num_sms](long long tiles) { return static_cast<double>((tiles + num_sms - 1) / num_sms); };
+  int best_mt = prefill_ts::MT_MAX;
+  double t_ts = 1e300;
+  for (int mt = prefill_ts::MT_MAX; mt >= 128; mt -= 32) {
+    const long long tiles = static_cast<long long>((M + mt - 1) / mt) * ((N + prefill_ts::NT - 1) / prefill_ts::NT);
+    const double t = waves(tiles) * kt * 0.82 * (0.7 + 0.3 * mt / 192.0);
+    if (t < t_ts * 0.999) {
+      t_ts = t;
+      best_mt = mt;
+    }
+  }
+  *ts_mt = best_mt;
+  if (force == W4A16_PREFILL_TMEM_A) return W4A16_PREFILL_TMEM_A;
+  if (force == W4A16_PREFILL_SMEM_B || M <= prefill::BMH) return W4A16_PREFILL_SMEM_B;
+  const int bn = choose_prefill_bn(M, N, num_sms, 2);
+  const long long ss_tiles = static_cast<long long>((M + prefill::BM - 1) / prefill::BM) * ((N + bn - 1) / bn);
+  const double t_ss = waves(ss_tiles) * kt * 1.12 * ss_step_model(bn, 2) / ss_step_model(prefill::BN_MAX, 2);
+  return t_ts < t_ss ? W4A16_PREFILL_TMEM_A : W4A16_PREFILL_SMEM_B;
+}
+
+int launch_prefill_ts(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
+                      const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
+                      long long ldy, cudaStream_t stream, int swiglu, int nat, int y_bf16, int mt) {
+  CUtensorMap tx, ty, tw, tsc, tz;
+  if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill_ts::BK,
+                   static_cast<uint32_t>(mt), CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, qw, N, K / 8, N, prefill_ts::NT, prefill_ts::BK / 8,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&tsc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s, N, K / G, N, prefill_ts::NT, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !make_map_2d(&tz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, z, N, K / G, N, prefill_ts::NT, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return W4A16_ERR_ALIGNMENT;
+  }
+  const bool y_aligned = aligned16(y) && (ldy % (y_f32 ? 4 : 8)) == 0;
+  const bool tma_store =
+      !swiglu && y_aligned && (y_f32 ? make_map_2d(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, N, M, ldy, 32, 32,
+                                                   CU_TENSOR_MAP_SWIZZLE_128B)
+                          : make_map_2d(&ty, y_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                        2, y, N, M, ldy, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B));
+  if (!tma_store) ty = tx;   // unused by the kernel
+  prefill_ts::Params p;
+  p.tma_store = tma_store ? 1 : 0;
+  p.bias = bias;
+  p.y = y;
+  p.y_f32 = y_f32;
+  p.y_bf16 = y_bf16;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.G = G;
+  p.g_shift = ((G & (G - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(G)) : -1;
+  p.ldy = ldy;
+  p.mt = mt;
+  p.m_tiles = (M + mt - 1) / mt;
+  p.n_tiles = (N + prefill_ts::NT - 1) / prefill_ts::NT;
+  p.dsets = 4 * mt + 128 <= static_cast<int>(prefill_ts::TMEM_COLS) ? 2 : 1;
+  p.a_col0 = p.dsets * 2 * mt;
+  p.astages = std::min(prefill_ts::AST_MAX, (static_cast<int>(prefill_ts::TMEM_COLS) - p.a_col0) / 64);
+  if (p.astages < 2) return W4A16_ERR_INVALID;
+  p.xstages = std::min(prefill_ts::TST_MAX, prefill_ts::X_RING_BYTES / (mt * prefill_ts::BK * 2));
+  p.idesc = umma_idesc_f16_f32(128, static_cast<uint32_t>(mt));
+  p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
+  const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
+  const dim3 blk(prefill_ts::THREADS);
+  if (swiglu && nat)
+    prefill_ts::w4a16_ts_kernel<true, true><<<grid, blk, prefill_ts::SMEM_BYTES, stream>>>(tx, ty, tw, tsc, tz, p);
+  else if (swiglu)
+    prefill_ts::w4a16_ts_kernel<true, false><<<grid, blk, prefill_ts::SMEM_BYTES, stream>>>(tx, ty, tw, tsc, tz, p);
+  else if (nat)
+    prefill_ts::w4a16_ts_kernel<false, true><<<grid, blk, prefill_ts::SMEM_BYTES, stream>>>(tx, ty, tw, tsc, tz, p);
+  else
+    prefill_ts::w4a16_ts_kernel<false, false><<<grid, blk, prefill_ts::SMEM_BYTES, stream>>>(tx, ty, tw, tsc, tz, p);
+  W4A16_RETURN_IF_LAUNCH_FAILED();
+  return W4A16_OK;
+}
+
 // h[m, n] = silu(g) * u with g = gate_up[m, n], u = gate_up[m, N + n]: the
 // SwiGLU between the fused gate/up projection and the down projection of an
 // MLP block, computed in fp32 and rounded once to fp16.
@@ -590,6 +699,10 @@ static int gemm_impl(const void* x, const int32_t* qweight, const void* scales, 
     return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g,
                              ldy, workspace, workspace_bytes, s, ArArgs(), swiglu, nat, y_bf16);
   }
+  int ts_mt = 0;
+  if (choose_prefill_kernel(static_cast<int>(M), n, k, dev->num_sms, &ts_mt) == W4A16_PREFILL_TMEM_A)
+    return launch_prefill_ts(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s, swiglu,
+                             nat, y_bf16, ts_mt);
   return launch_prefill(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s,
                         swiglu, nat, y_bf16);
 }
@@ -847,6 +960,13 @@ int w4a16_set_wait_budget_ns(int64_t ns) {
   if (ns < 0 || (ns > 0 && ns < 1000 * 1000) || ns > 600ll * 1000 * 1000 * 1000) return W4A16_ERR_INVALID;
   g_wait_budget_ns.store(ns == 0 ? kWaitBudgetNs : static_cast<unsigned long long>(ns),
                          std::memory_order_relaxed);
+  return W4A16_OK;
+}
+
+int w4a16_set_prefill_kernel(int which) {
+  if (which != W4A16_PREFILL_AUTO && which != W4A16_PREFILL_SMEM_B && which != W4A16_PREFILL_TMEM_A)
+    return W4A16_ERR_INVALID;
+  g_prefill_kernel.store(which, std::memory_order_relaxed);
   return W4A16_OK;
 }
 

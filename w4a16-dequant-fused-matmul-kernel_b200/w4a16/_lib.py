@@ -20,6 +20,7 @@ FLAG_KERNEL_ORDER = 1
 FLAG_SWIGLU = 2
 FLAG_F32_OUT = 4
 FLAG_BF16_OUT = 8
+PREFILL_AUTO, PREFILL_SMEM_B, PREFILL_TMEM_A = 0, 1, 2
 W4A16_ERR_TIMEOUT = -5
 W4A16_ERR_WORKSPACE = -6
 DTYPE_CODES = {torch.float16: 0, torch.float32: 1, torch.bfloat16: 2}
@@ -52,6 +53,7 @@ SIGNATURES = {
     "w4a16_dequantize": ([_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),
     "w4a16_check_device_errors": ([_vp, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
     "w4a16_set_wait_budget_ns": ([_c_i64], ctypes.c_int),
+    "w4a16_set_prefill_kernel": ([ctypes.c_int], ctypes.c_int),
     "w4a16_reset_scratch": ([_vp, _c_i64, _vp], ctypes.c_int),
     "w4a16_gemm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                             _vp], ctypes.c_int),
@@ -234,3 +236,10 @@ def set_wait_budget_ns(ns: int) -> None:
     """Time budget of every bounded wait in kernels launched from now on (0: the
     default 4 s). Launches already queued or captured keep their budget."""
     check(lib().w4a16_set_wait_budget_ns(int(ns)), "w4a16_set_wait_budget_ns")
+
+
+def set_prefill_kernel(which: int) -> None:
+    """Prefill (M > 32) kernel for launches from now on: PREFILL_AUTO (per-shape
+    choice), PREFILL_SMEM_B (dequantised weights as the shared-memory MMA operand) or
+    PREFILL_TMEM_A (dequantised weights in tensor memory). For tests and tuning."""
+    check(lib().w4a16_set_prefill_kernel(int(which)), "w4a16_set_prefill_kernel")
