@@ -20,8 +20,9 @@ same GEMM with the full Y on every rank, through the fused GEMM + all-gather
 kernel and through GEMM + NCCL all-gather), ``mlp_stack`` (80 decoder MLP blocks,
 gate/up column-parallel with SwiGLU fused into its epilogue, down row-parallel with
 its all-reduce, M=1 and M=2048),
-``prefill`` (N = 1: M in {512,2048,4096,8192} at K=4096, N=14336 on the tcgen05
-kernel; ``secondary`` repeats M=4096). Each has a roofline against the measured
+``prefill`` (N = 1: M in {512,2048,4096,8192} at K=4096, N=14336 on the prefill
+kernel the per-shape choice picks, with the other prefill kernel's time beside it;
+``secondary`` repeats M=4096). Each has a roofline against the measured
 peaks. Before anything is timed, every rank checks its outputs (its shard, the
 gathered Y, the MLP block's activations and reduced output) against the numpy
 oracle on sampled columns; a mismatch on any rank ends the run non-zero.
@@ -574,11 +575,16 @@ def measure_mlp(ctx, args):
     return lines, ok
 
 
+PREFILL_KERNELS = {1: "prefill::w4a16_tcgen05_kernel (weights as the shared-memory operand)",
+                   2: "prefill_ts::w4a16_ts_kernel (weights as the TMEM operand)"}
+
+
 def measure_prefill(ctx, args):
     """N = 1: the tcgen05 prefill GEMM at M in {512, 2048, 4096, 8192}, K=4096, N=14336,
     L2 flushed before every timed launch; oracle-checked on sampled rows and columns."""
     torch = ctx.torch
     import w4a16
+    from w4a16 import _lib
     c = PREFILL
     K, N, G = c["K"], c["N"], c["G"]
     W = make_weight(torch, K, N, c["sigma"], 0.0, 99, ctx.dev)
@@ -613,9 +619,30 @@ def measure_prefill(ctx, args):
             times.append(a.elapsed_time(b))
         t = statistics.median(times) / 1e3
         flops = 2.0 * M * N * K
+        which = _lib.prefill_choice(M, N, K)
+        # the other prefill kernel on the same shape, for the record (forced, same timing)
+        other = _lib.PREFILL_SMEM_B if which == _lib.PREFILL_TMEM_A else _lib.PREFILL_TMEM_A
+        _lib.set_prefill_kernel(other)
+        try:
+            w4a16.w4a16_matmul(X, qw, s, z, G, out=y)
+            alt = []
+            for _ in range(iters):
+                flush.zero_()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                w4a16.w4a16_matmul(X, qw, s, z, G, out=y)
+                b.record()
+                torch.cuda.synchronize(ctx.dev)
+                alt.append(a.elapsed_time(b))
+        finally:
+            _lib.set_prefill_kernel(_lib.PREFILL_AUTO)
+        t_alt = statistics.median(alt) / 1e3
         out.append({"M": M, "K": K, "N": N, "us": t * 1e6, "tflops": flops / t / 1e12, "iters": iters,
-                    "oracle_max_abs_err": err,
-                    "roofline": tensor_roofline(flops, t, ctx.pk, "prefill::w4a16_tcgen05_kernel")})
+                    "kernel": PREFILL_KERNELS[which], "oracle_max_abs_err": err,
+                    "other_kernel": {"kernel": PREFILL_KERNELS[other], "us": t_alt * 1e6,
+                                     "tflops": flops / t_alt / 1e12},
+                    "roofline": tensor_roofline(flops, t, ctx.pk, PREFILL_KERNELS[which])})
         del X, y
     return out, ok
 
@@ -810,6 +837,7 @@ def run_ours(args):
             extra["secondary"] = {
                 "metric": "W4A16 GEMM TFLOP/s at M=4096, K=4096, N=14336, G=128 (tcgen05 prefill kernel)",
                 "value": p["tflops"], "unit": "TFLOP/s", "ms": p["us"] / 1e3, "iters": p["iters"],
+                "kernel": p["kernel"],
                 "l2": "L2 flushed (252 MiB write) before every timed launch", "roofline": p["roofline"]}
     assert _lib.check_device_errors(dev) == 0
     if not ctx.all_ok(all_ok):

@@ -273,6 +273,10 @@ int w4a16_set_wait_budget_ns(int64_t ns);
 #define W4A16_PREFILL_SMEM_B 1
 #define W4A16_PREFILL_TMEM_A 2
 int w4a16_set_prefill_kernel(int which);
+/* The prefill kernel (W4A16_PREFILL_SMEM_B or _TMEM_A) the current selection gives an
+ * M x N x K GEMM with N % 8 == 0 on the current device, or W4A16_PREFILL_AUTO when M <= 32
+ * (decode). For reports and tests; no reference counterpart. */
+int w4a16_prefill_choice(int64_t M, int64_t N, int64_t K, int* which);
 
 /*
  * After W4A16_ERR_TIMEOUT: zero `workspace_bytes` of a caller's GEMM workspace

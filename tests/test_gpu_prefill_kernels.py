@@ -123,3 +123,17 @@ def test_prefill_kernels_agree_at_size():
 def test_prefill_kernel_selection_rejects_unknown():
     with pytest.raises(RuntimeError):
         _lib.set_prefill_kernel(7)
+
+
+def test_prefill_choice_query():
+    """The per-shape choice: decode sizes report AUTO; a forced kernel is what the
+    query reports; the automatic choice is one of the two kernels."""
+    assert _lib.prefill_choice(32, 4096, 4096) == _lib.PREFILL_AUTO
+    for M in (33, 512, 4096):
+        assert _lib.prefill_choice(M, 14336, 4096) in (_lib.PREFILL_SMEM_B, _lib.PREFILL_TMEM_A)
+    try:
+        for which in KERNELS.values():
+            _lib.set_prefill_kernel(which)
+            assert _lib.prefill_choice(4096, 14336, 4096) == which
+    finally:
+        _lib.set_prefill_kernel(_lib.PREFILL_AUTO)

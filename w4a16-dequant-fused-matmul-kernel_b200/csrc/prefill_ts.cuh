@@ -197,7 +197,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t dcol = tmem_base + static_cast<uint32_t>(d.slot * 2 * mt);
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&tfull[t.slot], t.phase, p.wait_ns) || !mbar_wait(&afull[a.slot], a.phase, p.wait_ns)) {
+          // afull also implies this step's x tile has landed (the first dequantiser warp
+          // waits for it before arriving): one wait per step on this thread's path
+          if (!mbar_wait(&afull[a.slot], a.phase, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -261,7 +263,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int kp = dw >> 3;               // words 4kp..4kp+3 of the step
     const int nloc = h * 128 + q * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-    Ring wr, ar;
+    Ring wr, ar, xr;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       for (int kt = 0; kt < KT; ++kt) {
@@ -310,6 +312,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_st_32x32b_x16(tmem_base + lane_addr + static_cast<uint32_t>(p.a_col0 + ar.slot * 64 + h * 32 + kp * 16), v);
         tmem_st_wait();
         tc_fence_before();
+        if (warp == DQ_WARP0) {
+          // the MMA issuer waits only on afull: this warp's arrival also vouches for the x tile
+          if (!warp_wait(&tfull[xr.slot], xr.phase, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+          xr.advance(p.xstages);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[ar.slot]);
         ar.advance(p.astages);

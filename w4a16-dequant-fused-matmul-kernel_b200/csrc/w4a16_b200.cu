@@ -963,6 +963,19 @@ int w4a16_set_wait_budget_ns(int64_t ns) {
   return W4A16_OK;
 }
 
+int w4a16_prefill_choice(int64_t M, int64_t N, int64_t K, int* which) {
+  if (which == nullptr || M <= 0 || N <= 0 || K <= 0 || M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff)
+    return W4A16_ERR_INVALID;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  int mt = 0;
+  *which = M <= 32 ? W4A16_PREFILL_AUTO
+                   : choose_prefill_kernel(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                           dev->num_sms, &mt);
+  return W4A16_OK;
+}
+
 int w4a16_set_prefill_kernel(int which) {
   if (which != W4A16_PREFILL_AUTO && which != W4A16_PREFILL_SMEM_B && which != W4A16_PREFILL_TMEM_A)
     return W4A16_ERR_INVALID;

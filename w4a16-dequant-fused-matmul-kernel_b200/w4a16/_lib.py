@@ -54,6 +54,7 @@ SIGNATURES = {
     "w4a16_check_device_errors": ([_vp, ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
     "w4a16_set_wait_budget_ns": ([_c_i64], ctypes.c_int),
     "w4a16_set_prefill_kernel": ([ctypes.c_int], ctypes.c_int),
+    "w4a16_prefill_choice": ([_c_i64, _c_i64, _c_i64, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "w4a16_reset_scratch": ([_vp, _c_i64, _vp], ctypes.c_int),
     "w4a16_gemm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                             _vp], ctypes.c_int),
@@ -243,3 +244,11 @@ def set_prefill_kernel(which: int) -> None:
     choice), PREFILL_SMEM_B (dequantised weights as the shared-memory MMA operand) or
     PREFILL_TMEM_A (dequantised weights in tensor memory). For tests and tuning."""
     check(lib().w4a16_set_prefill_kernel(int(which)), "w4a16_set_prefill_kernel")
+
+
+def prefill_choice(M: int, N: int, K: int) -> int:
+    """The prefill kernel the current selection gives an M x N x K GEMM on the current
+    device (PREFILL_SMEM_B or PREFILL_TMEM_A; PREFILL_AUTO when M <= 32)."""
+    which = ctypes.c_int(0)
+    check(lib().w4a16_prefill_choice(int(M), int(N), int(K), ctypes.byref(which)), "w4a16_prefill_choice")
+    return which.value
