@@ -218,6 +218,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   return false;
 }
 
+// mbar_wait that sleeps `sleep_ns` between polls: for roles whose waits are long or
+// off the critical path (an epilogue waiting for a tile's accumulators, dequantisers
+// running ahead of the MMAs), so that their polling leaves the issue slots to the
+// warps doing work -- on a busy SM a spinning poller slows the MMA issuer's own waits.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, uint64_t budget_ns,
+                                                  uint32_t sleep_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 7u) == 0u && global_timer_ns() - t0 > budget_ns) break;
+  }
+  flag_error(kErrWaitTimeout);
+  return false;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------

@@ -119,13 +119,20 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, 
 }
 
 // Lane 0 waits, the warp follows: keeps mbarrier polling off the shared-memory pipe.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint64_t budget_ns) {
+// sleep_ns > 0 backs the polling off (mbar_wait_backoff).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint64_t budget_ns,
+                                          uint32_t sleep_ns = 0) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, budget_ns);
+  if ((threadIdx.x & 31) == 0)
+    ok = sleep_ns ? mbar_wait_backoff(bar, parity, budget_ns, sleep_ns) : mbar_wait(bar, parity, budget_ns);
   ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
   __syncwarp();
   return ok;
 }
+
+// Polling back-off of the roles that wait off the MMA issuer's critical path.
+constexpr uint32_t kEpilogueSleepNs = 512;    // a tile's K loop lasts tens of microseconds
+constexpr uint32_t kRunAheadSleepNs = 128;    // producers and dequantisers ahead of the MMAs
 
 struct Ring {
   int slot = 0;
@@ -200,7 +207,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tile_coords(p, tile, mt, nt);
         const int m0 = mt * p.bm;
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u, p.wait_ns)) { ok = false; break; }
+          if (!mbar_wait_backoff(&tempty[r.slot], r.phase ^ 1u, p.wait_ns, kRunAheadSleepNs)) { ok = false; break; }
           uint8_t* st = tring + r.slot * T_BYTES;
           mbar_arrive_expect_tx(&tfull[r.slot], p.halves * (A_BYTES / 2));   // the x box is [bm x 64]
           tma_load_2d(st, &tm_x, &tfull[r.slot], kt * BK, m0);
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       fetch(1, nxt);
       for (int kt = 0; kt < KT; ++kt) {
         fetch(kt + 2, nnx);
-        if (!warp_wait(&bempty[br.slot], br.phase ^ 1u, p.wait_ns)) {
+        if (!warp_wait(&bempty[br.slot], br.phase ^ 1u, p.wait_ns, kRunAheadSleepNs)) {
           ok = false;
           break;
         }
@@ -341,7 +348,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (p.tma_store && lane == 0) tma_prefetch_desc(&tm_y);
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
-      if (!warp_wait(accfull, local & 1, p.wait_ns)) break;
+      if (!warp_wait(accfull, local & 1, p.wait_ns, kEpilogueSleepNs)) break;
       tc_fence_after();
       int mt, nt;
       tile_coords(p, tile, mt, nt);

@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         int mi, ni;
         prefill::tile_coords_mn(p.m_tiles, p.n_tiles, tile, mi, ni);
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&tempty[r.slot], r.phase ^ 1u, p.wait_ns)) { ok = false; break; }
+          if (!mbar_wait_backoff(&tempty[r.slot], r.phase ^ 1u, p.wait_ns, prefill::kRunAheadSleepNs)) { ok = false; break; }
           uint8_t* st = xring + r.slot * (mt * BK * 2);
           mbar_arrive_expect_tx(&tfull[r.slot], static_cast<uint32_t>(mt * BK * 2));   // the x box is [mt x 64]
           tma_load_2d(st, &tm_x, &tfull[r.slot], kt * BK, mi * mt);
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         int mi, ni;
         prefill::tile_coords_mn(p.m_tiles, p.n_tiles, tile, mi, ni);
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(&wempty[r.slot], r.phase ^ 1u, p.wait_ns)) { ok = false; break; }
+          if (!mbar_wait_backoff(&wempty[r.slot], r.phase ^ 1u, p.wait_ns, prefill::kRunAheadSleepNs)) { ok = false; break; }
           uint8_t* st = wring + r.slot * W_BYTES;
           const int kk = kt * BK;
           const int grow = p.g_shift >= 0 ? kk >> p.g_shift : kk / p.G;
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
       for (int kt = 0; kt < KT; ++kt) {
-        if (!warp_wait(&wfull[wr.slot], wr.phase, p.wait_ns)) {
+        if (!warp_wait(&wfull[wr.slot], wr.phase, p.wait_ns, prefill::kRunAheadSleepNs)) {
           ok = false;
           break;
         }
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&wempty[wr.slot]);
         wr.advance(WSTAGES);
-        if (!warp_wait(&aempty[ar.slot], ar.phase ^ 1u, p.wait_ns)) {
+        if (!warp_wait(&aempty[ar.slot], ar.phase ^ 1u, p.wait_ns, prefill::kRunAheadSleepNs)) {
           ok = false;
           break;
         }
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_before();
         if (warp == DQ_WARP0) {
           // the MMA issuer waits only on afull: this warp's arrival also vouches for the x tile
-          if (!warp_wait(&tfull[xr.slot], xr.phase, p.wait_ns)) {
+          if (!warp_wait(&tfull[xr.slot], xr.phase, p.wait_ns, prefill::kRunAheadSleepNs)) {
             ok = false;
             break;
           }
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (p.tma_store && lane == 0) tma_prefetch_desc(&tm_y);
     Ring d;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      if (!warp_wait(&accfull[d.slot], d.phase, p.wait_ns)) break;
+      if (!warp_wait(&accfull[d.slot], d.phase, p.wait_ns, prefill::kEpilogueSleepNs)) break;
       tc_fence_after();
       int mi, ni;
       prefill::tile_coords_mn(p.m_tiles, p.n_tiles, tile, mi, ni);
