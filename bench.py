@@ -651,7 +651,8 @@ def measure_e2e(ctx, args, X, copies, R, G, n):
     """The headline through the public API with host buffers (see the module docstring):
     (a) pipelined, the K steps replayed from one CUDA graph, x staged in by
     w4a16.stage_copy (a kernel, so the GEMM after it still starts under programmatic
-    dependent launch) and y copied out on a second stream; (b) eager from Python."""
+    dependent launch) and y copied out on a second stream; (b) eager from Python with
+    Tensor.copy_ in and out; (c) eager from Python through w4a16.w4a16_matmul_host."""
     torch = ctx.torch
     import w4a16
     M, K = X.shape
@@ -716,14 +717,36 @@ def measure_e2e(ctx, args, X, copies, R, G, n):
         torch.cuda.synchronize(dev)
         ctx.barrier()
         s0e.record(stream)
+        h0 = time.perf_counter()
         for i in range(args.steps):
             Xd[0].copy_(Xh, non_blocking=True)
             yy = w4a16.w4a16_matmul(Xd[0], *copies[i % R], G)
             Yh.copy_(yy, non_blocking=True)
+        ctx.host_submit_copies_us = (time.perf_counter() - h0) * 1e6 / args.steps
         s1e.record(stream)
     torch.cuda.synchronize(dev)
     t_eager = ctx.max_over_ranks(s0e.elapsed_time(s1e))
-    return t_pipe, t_eager
+
+    # (c) eager through w4a16.w4a16_matmul_host: one call per step, pinned x in and
+    # pinned y out (stage-in, GEMM, stage-out kernels chained on the GEMM stream)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            w4a16.w4a16_matmul_host(Xh, *copies[i % R], G, out=Yh)
+        torch.cuda.synchronize(dev)
+        ctx.barrier()
+        s0e.record(stream)
+        h0 = time.perf_counter()
+        for i in range(args.steps):
+            w4a16.w4a16_matmul_host(Xh, *copies[i % R], G, out=Yh)
+        h1 = time.perf_counter()
+        s1e.record(stream)
+    torch.cuda.synchronize(dev)
+    t_host = ctx.max_over_ranks(s0e.elapsed_time(s1e))
+    ctx.host_submit_us = (h1 - h0) * 1e6 / args.steps
+    y_last = w4a16.w4a16_matmul(X, *copies[(args.steps - 1) % R], G)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(Yh.to(dev), y_last), "e2e: w4a16_matmul_host's y differs from the GEMM's result"
+    return t_pipe, t_eager, t_host
 
 
 def run_ours(args):
@@ -804,9 +827,10 @@ def run_ours(args):
                          "what": "the headline GEMM with qweight repacked once into the kernel nibble order"}
     del kcopies, yk
 
-    t_pipe, t_eager = measure_e2e(ctx, args, X, hw.copies, hw.R, G, n)
+    t_pipe, t_eager, t_host = measure_e2e(ctx, args, X, hw.copies, hw.R, G, n)
     e2e_value = world * rank_bytes * args.steps / (t_pipe / 1e3) / 1e9
     e2e_eager = world * rank_bytes * args.steps / (t_eager / 1e3) / 1e9
+    e2e_host = world * rank_bytes * args.steps / (t_host / 1e3) / 1e9
     del hw, y
     torch.cuda.empty_cache()
 
@@ -868,8 +892,17 @@ def run_ours(args):
                         "(this rank's columns) every step: x staged in by a kernel on the GEMM stream "
                         "(chains under programmatic dependent launch), y copied out on a second stream "
                         "while the next steps compute; the K steps replayed from one CUDA graph",
-                "eager": {"value": e2e_eager, "unit": "GB/s",
-                          "path": "the same three calls per step from Python on one stream"}},
+                "eager": {"value": e2e_host, "unit": "GB/s", "us_per_step": t_host * 1e3 / args.steps,
+                          "host_submit_us_per_step": ctx.host_submit_us,
+                          "path": "eager from Python, one w4a16.w4a16_matmul_host call per step (pinned X "
+                                  "in, pinned Y out: stage-in, GEMM and stage-out kernels chained under "
+                                  "programmatic dependent launch on one stream)"},
+                "eager_torch_copies": {"value": e2e_eager, "unit": "GB/s",
+                                       "us_per_step": t_eager * 1e3 / args.steps,
+                                       "host_submit_us_per_step": ctx.host_submit_copies_us,
+                                       "path": "eager from Python on one stream: Tensor.copy_ of X in, "
+                                               "w4a16.w4a16_matmul, Tensor.copy_ of Y out (copy-engine "
+                                               "transfers between the kernels)"}},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "kernel_order": kernel_order_line,

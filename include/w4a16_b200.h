@@ -182,6 +182,25 @@ int w4a16_repack(const int32_t* qweight, int32_t* out, int64_t K, int64_t N,
 int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* stream);
 
 /*
+ * w4a16_gemm_ex on host-resident activations: x_host [M, K] fp16 is staged into the
+ * device buffer x_dev, the GEMM writes the device buffer y_dev [M, n] (n = N, or N/2
+ * with W4A16_FLAG_SWIGLU; fp32 with W4A16_FLAG_F32_OUT, bf16 with
+ * W4A16_FLAG_BF16_OUT, else fp16), and y_dev is staged out to y_host: kernels on
+ * `stream` chained under programmatic dependent launch (no copy-engine transfers
+ * between them), so an eager loop of calls keeps the GEMM's start overlapped with
+ * its predecessor. Up to 32 tokens the GEMM writes y_host directly (y_dev unused). x_host and y_host must be pinned host memory
+ * mapped into the device's address space (W4A16_ERR_INVALID otherwise); all four
+ * buffers 16-byte aligned, M*K*2 and the y bytes multiples of 16
+ * (W4A16_ERR_ALIGNMENT). y_host holds the result once the stream has completed.
+ * x_dev/y_dev may be reused by the next call on the same stream. No reference
+ * counterpart (the reference's GEMM takes device tensors).
+ */
+int w4a16_gemm_host(const void* x_host, const int32_t* qweight, const void* scales, const void* zeros,
+                    const void* bias, void* y_host, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                    uint32_t flags, void* x_dev, void* y_dev, void* workspace, int64_t workspace_bytes,
+                    void* stream);
+
+/*
  * Bytes of workspace w4a16_gemm needs for this shape on the current device
  * (0 for shapes whose kernels need none). No reference counterpart: the
  * reference's kernels never split K across thread blocks.

@@ -255,6 +255,38 @@ def test_column_slices_of_a_wider_output(M, pad):
         assert torch.all(buf[:, 2 * N:] == 7.0), "a store landed outside the shards"
 
 
+# ---------------------------- host-resident activations (w4a16.w4a16_matmul_host) --
+@pytest.mark.parametrize("M,K,N,G", [(1, 4096, 11008, 128), (5, 1024, 264, 64), (32, 2048, 512, 128),
+                                     (300, 1024, 520, 128)])
+def test_matmul_host_matches_device_path(M, K, N, G):
+    """Pinned x in, pinned y out through one call (stage in, GEMM, stage out): the same
+    bits as the device GEMM on the same inputs, with and without bias and in the
+    kernel nibble order; repeated calls reuse the staging buffers."""
+    X, qw, s, z = _build(M, K, N, G, sigma=0.05, seed=M + N)
+    bias = torch.randn(N, device="cuda").half()
+    xh = X.cpu().pin_memory()
+    yh = torch.empty(M, N, dtype=torch.float16).pin_memory()
+    for b in (None, bias):
+        want = w4a16_matmul(X, qw, s, z, G, bias=b)
+        for _ in range(2):
+            yh.fill_(0)
+            w4a16.w4a16_matmul_host(xh, qw, s, z, G, out=yh, bias=b)
+            torch.cuda.current_stream().synchronize()
+            assert torch.equal(yh.cuda(), want)
+    qk = w4a16.repack_qweight(qw)
+    got = w4a16.w4a16_matmul_host(xh, qk, s, z, G, kernel_order=True)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(got.cuda(), w4a16_matmul(X, qk, s, z, G, kernel_order=True))
+
+
+def test_matmul_host_rejects_unpinned_and_device_inputs():
+    X, qw, s, z = _build(4, 256, 64, 64)
+    with pytest.raises(AssertionError):
+        w4a16.w4a16_matmul_host(X, qw, s, z, 64)               # x on the device
+    with pytest.raises(w4a16.W4A16Error):
+        w4a16.w4a16_matmul_host(X.cpu(), qw, s, z, 64)         # x not pinned: the C ABI refuses it
+
+
 # ---------------------------- staging copies (w4a16.stage_copy) --------------------
 def test_stage_copy_host_device_and_back():
     from w4a16 import stage_copy

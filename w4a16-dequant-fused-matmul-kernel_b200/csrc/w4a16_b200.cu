@@ -788,17 +788,10 @@ int w4a16_repack(const int32_t* qweight, int32_t* out, int64_t K, int64_t N, int
   return W4A16_OK;
 }
 
-int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* stream) {
-  if (bytes < 0 || (bytes & 15) != 0) return W4A16_ERR_INVALID;
-  if (bytes == 0) return W4A16_OK;
-  if (src == nullptr || dst == nullptr) return W4A16_ERR_INVALID;
-  if (!aligned16(src) || !aligned16(dst)) return W4A16_ERR_ALIGNMENT;
-  DeviceState* dev = nullptr;
-  int st = current_device_state(&dev);
-  if (st != W4A16_OK) return st;
-  const void* s = device_reachable(src);
-  void* d = const_cast<void*>(device_reachable(dst));
-  if (s == nullptr || d == nullptr) return W4A16_ERR_INVALID;
+}  // extern "C"
+
+// The staging kernel between two device-visible addresses (checked by the caller).
+static int launch_stage(const void* s, void* d, int64_t bytes, int src_ready, void* stream) {
   const int64_t n16 = bytes / 16;
   const int64_t per_cta = static_cast<int64_t>(STAGE_THREADS) * STAGE_PER_THREAD;
   const int64_t blocks = (n16 + per_cta - 1) / per_cta;
@@ -819,6 +812,22 @@ int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* 
     return W4A16_ERR_LAUNCH;
   }
   return W4A16_OK;
+}
+
+extern "C" {
+
+int w4a16_stage(const void* src, void* dst, int64_t bytes, int src_ready, void* stream) {
+  if (bytes < 0 || (bytes & 15) != 0) return W4A16_ERR_INVALID;
+  if (bytes == 0) return W4A16_OK;
+  if (src == nullptr || dst == nullptr) return W4A16_ERR_INVALID;
+  if (!aligned16(src) || !aligned16(dst)) return W4A16_ERR_ALIGNMENT;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  const void* s = device_reachable(src);
+  void* d = const_cast<void*>(device_reachable(dst));
+  if (s == nullptr || d == nullptr) return W4A16_ERR_INVALID;
+  return launch_stage(s, d, bytes, src_ready, stream);
 }
 
 static int quantize_impl(const void* w, int w_dtype, int32_t* qweight, void* scales, void* zeros,
@@ -961,6 +970,39 @@ int w4a16_set_wait_budget_ns(int64_t ns) {
   g_wait_budget_ns.store(ns == 0 ? kWaitBudgetNs : static_cast<unsigned long long>(ns),
                          std::memory_order_relaxed);
   return W4A16_OK;
+}
+
+int w4a16_gemm_host(const void* x_host, const int32_t* qweight, const void* scales, const void* zeros,
+                    const void* bias, void* y_host, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                    uint32_t flags, void* x_dev, void* y_dev, void* workspace, int64_t workspace_bytes,
+                    void* stream) {
+  if (M < 0 || N < 0 || K <= 0) return W4A16_ERR_INVALID;
+  if (M == 0 || N == 0) return W4A16_OK;
+  if (x_host == nullptr || y_host == nullptr || x_dev == nullptr || y_dev == nullptr) return W4A16_ERR_INVALID;
+  const int64_t ncols = (flags & W4A16_FLAG_SWIGLU) ? N / 2 : N;
+  const int64_t esize = (flags & W4A16_FLAG_F32_OUT) ? 4 : 2;
+  const int64_t xbytes = M * K * 2, ybytes = M * ncols * esize;
+  if ((xbytes & 15) != 0 || (ybytes & 15) != 0) return W4A16_ERR_ALIGNMENT;
+  if (!aligned16(x_host) || !aligned16(y_host) || !aligned16(x_dev) || !aligned16(y_dev))
+    return W4A16_ERR_ALIGNMENT;
+  DeviceState* dev = nullptr;
+  int st = current_device_state(&dev);
+  if (st != W4A16_OK) return st;
+  const void* xs = device_reachable(x_host);
+  void* yd = const_cast<void*>(device_reachable(y_host));
+  if (xs == nullptr || yd == nullptr) return W4A16_ERR_INVALID;
+  // x in (read at once: the host filled it before the call), the GEMM, y out (after
+  // the GEMM): kernels chained under programmatic dependent launch. Up to 32 tokens the
+  // GEMM (decode or plain-load kernel, plain stores) writes y straight into the mapped
+  // host buffer and no stage-out kernel is needed; the prefill kernels store y with TMA,
+  // which needs device memory.
+  st = launch_stage(xs, x_dev, xbytes, 1, stream);
+  if (st != W4A16_OK) return st;
+  const bool direct = M <= 32;
+  st = gemm_impl(x_dev, qweight, scales, zeros, bias, direct ? yd : y_dev, 0, M, N, K, group_size, ncols,
+                 workspace, workspace_bytes, stream, flags);
+  if (st != W4A16_OK || direct) return st;
+  return launch_stage(y_dev, yd, ybytes, 0, stream);
 }
 
 int w4a16_prefill_choice(int64_t M, int64_t N, int64_t K, int* which) {

@@ -19,7 +19,7 @@ from __future__ import annotations
 
 from ._lib import W4A16Error, check_device_errors
 from .gemm import (interleave_gate_up, repack_qweight, stage_copy, swiglu, to_fp16, w4a16_matmul,
-                   w4a16_matmul_bf16, w4a16_matmul_f32, w4a16_matmul_swiglu)
+                   w4a16_matmul_bf16, w4a16_matmul_f32, w4a16_matmul_host, w4a16_matmul_swiglu)
 from .linear import W4A16Linear
 from .quant import dequantize_weight, pack_int4, quantize_weight, unpack_int4
 from .reference import dequant_then_matmul, fp16_matmul, reference_w4a16
@@ -42,6 +42,7 @@ __all__ = [
     "w4a16_matmul_bf16",
     "to_fp16",
     "stage_copy",
+    "w4a16_matmul_host",
     "W4A16Error",
     "check_device_errors",
 ]

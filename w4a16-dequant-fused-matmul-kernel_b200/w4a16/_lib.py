@@ -43,6 +43,7 @@ SIGNATURES = {
     "w4a16_gemm_swiglu": ([_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
                            _vp], ctypes.c_int),
     "w4a16_stage": ([_vp, _vp, _c_i64, ctypes.c_int, _vp], ctypes.c_int),
+    "w4a16_gemm_host": ([_vp] * 6 + [_c_i64] * 4 + [ctypes.c_uint32] + [_vp] * 3 + [_c_i64, _vp], ctypes.c_int),
     "w4a16_gemm_workspace_size": ([_c_i64, _c_i64, _c_i64, _c_i64, ctypes.POINTER(_c_i64)],
                                   ctypes.c_int),
     "w4a16_quantize": ([_vp, ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp], ctypes.c_int),

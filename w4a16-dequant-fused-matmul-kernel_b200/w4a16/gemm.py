@@ -326,6 +326,75 @@ def stage_copy(dst: Tensor, src: Tensor, src_ready: bool = False) -> Tensor:
     return dst
 
 
+_host_scratch: dict[int, tuple] = {}
+
+
+def _device_scratch(d: int, xbytes: int, ybytes: int) -> tuple[int, int]:
+    """Grow-only per-device staging buffers of :func:`w4a16_matmul_host` (256-byte
+    aligned allocations; the next call on the stream may reuse them)."""
+    ent = _host_scratch.get(d)
+    if ent is None or ent[0] < xbytes or ent[1] < ybytes:
+        xb = max(xbytes, 0 if ent is None else ent[0])
+        yb = max(ybytes, 0 if ent is None else ent[1])
+        bufs = (torch.empty(xb, dtype=torch.uint8, device=d), torch.empty(yb, dtype=torch.uint8, device=d))
+        ent = (xb, yb, bufs[0].data_ptr(), bufs[1].data_ptr(), bufs)
+        _host_scratch[d] = ent
+    return ent[2], ent[3]
+
+
+def w4a16_matmul_host(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
+                      out: Tensor | None = None, *, bias: Tensor | None = None,
+                      kernel_order: bool = False) -> Tensor:
+    """The fused GEMM on host-resident activations: ``x`` is a pinned CPU fp16
+    [M, K] tensor, the weights live on a CUDA device, and the fp16 [M, N] result is
+    written into the pinned CPU tensor ``out`` (allocated pinned when omitted, which
+    is slow: pass ``out`` in a loop). One C call stages x in, runs the GEMM and stages
+    y out as three kernels chained under programmatic dependent launch on the
+    weights' device's current stream; ``out`` holds the result once that stream has
+    completed (e.g. ``torch.cuda.current_stream(dev).synchronize()``). Host memory
+    that is not pinned raises :class:`W4A16Error`. No reference counterpart: an eager
+    serving loop on host buffers without copy-engine round trips.
+    """
+    d = qweight.get_device()
+    xs, qs = x.shape, qweight.shape
+    # the common case in one expression; anything else gets the specific assertion
+    if not (d >= 0 and not x.is_cuda and len(xs) == 2 and len(qs) == 2 and x.dtype is _F16
+            and qweight.dtype is _I32 and scales.dtype is _F16 and zeros.dtype is _F16
+            and qs[0] * 8 == xs[1] and group_size > 0 and xs[1] % group_size == 0
+            and group_size % _BLOCK_K_RULE == 0 and scales.shape == (xs[1] // group_size, qs[1])
+            and zeros.shape == scales.shape and scales.get_device() == d and zeros.get_device() == d
+            and x.is_contiguous() and qweight.is_contiguous() and scales.is_contiguous()
+            and zeros.is_contiguous()):
+        assert d >= 0, "qweight must be on a CUDA device"
+        assert not x.is_cuda, "x must be a pinned CPU tensor"
+        assert x.dim() == 2 and x.dtype is _F16 and x.is_contiguous(), "x must be a contiguous fp16 [M, K] tensor"
+        w4a16_matmul(torch.empty((0, xs[1]), device=d, dtype=_F16), qweight, scales, zeros, group_size)
+    M, K = xs
+    N = qs[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=_F16, pin_memory=True)
+    else:
+        assert not out.is_cuda and out.shape == (M, N) and out.dtype is _F16 and out.is_contiguous(), (
+            f"out must be a contiguous pinned CPU fp16 [{M}, {N}] tensor")
+    if bias is not None:
+        assert bias.get_device() == d and bias.dtype is _F16 and bias.shape == (N,) and bias.is_contiguous()
+    if M == 0 or N == 0:
+        return out
+    if d != _current_device():
+        with torch.cuda.device(d):
+            return w4a16_matmul_host(x, qweight, scales, zeros, group_size, out, bias=bias, kernel_order=kernel_order)
+    stream = _raw_stream(d)
+    ws_ptr, ws_bytes = _lib.workspace_for(M, N, K, group_size, d, stream)
+    x_dev, y_dev = _device_scratch(d, M * K * 2, M * N * 2)
+    st = _lib.lib().w4a16_gemm_host(
+        x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), zeros.data_ptr(),
+        None if bias is None else bias.data_ptr(), out.data_ptr(), M, N, K, group_size,
+        _lib.FLAG_KERNEL_ORDER if kernel_order else 0, x_dev, y_dev, ws_ptr, ws_bytes, stream)
+    if st:
+        _lib.check(st, "w4a16_gemm_host")
+    return out
+
+
 def w4a16_matmul_into(x: Tensor, qweight: Tensor, scales: Tensor, zeros: Tensor, group_size: int,
                       y: Tensor, ldy: int, bias: Tensor | None = None) -> None:
     """Low-level variant: write ``Y`` into rows of pitch ``ldy`` starting at
