@@ -230,7 +230,7 @@ def _fused_row_rank(rank: int, world: int, port: int, q) -> None:
         q.put((rank, None, None, None, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_multi_gpu_fused_row_parallel_gemm_allreduce(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -347,7 +347,7 @@ def _fused_col_rank(rank: int, world: int, port: int, q) -> None:
         q.put((rank, None, None, None, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_multi_gpu_fused_column_parallel_gemm_allgather(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
