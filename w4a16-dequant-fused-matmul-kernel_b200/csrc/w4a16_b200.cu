@@ -445,10 +445,12 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
 //     choose_prefill_bn scales it);
 //   TMEM-operand kernel, 256 weight columns x mt tokens: ~0.82 us at mt = 192, ~0.7 of
 //     it independent of mt.
+//   shared-memory operand kernel, single 128-row half (M <= 128): ~1.07 us per step,
+//     latency-bound (its dequantisers prefetch only two steps ahead), whatever bn.
 // The TMEM-operand tile does ~1.17x the work per unit time, so it wins unless its
-// coarser wave quantisation loses more (M = 512; N = 8192 at M = 2048). Up to 128
-// tokens the single-half shared-memory tile is kept (it spreads one row of tiles).
-// w4a16_set_prefill_kernel() overrides the choice (tests exercise both kernels).
+// coarser wave quantisation loses more (M = 512; N = 8192 at M = 2048). At 33-128
+// tokens it takes 56 vs 68.5 us (K=4096, N=14336) and 101-104 vs 138 us (K=8192,
+// N=28672). w4a16_set_prefill_kernel() overrides the choice (tests exercise both).
 std::atomic<int> g_prefill_kernel{W4A16_PREFILL_AUTO};
 
 double ss_step_model(int bn, int halves) {
@@ -461,7 +463,7 @@ int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt) {
   auto waves = [num_sms](long long tiles) { return static_cast<double>((tiles + num_sms - 1) / num_sms); };
   int best_mt = prefill_ts::MT_MAX;
   double t_ts = 1e300;
-  for (int mt = prefill_ts::MT_MAX; mt >= 128; mt -= 32) {
+  for (int mt = prefill_ts::MT_MAX; mt >= prefill_ts::MT_MIN; mt -= 32) {
     const long long tiles = static_cast<long long>((M + mt - 1) / mt) * ((N + prefill_ts::NT - 1) / prefill_ts::NT);
     const double t = waves(tiles) * kt * 0.82 * (0.7 + 0.3 * mt / 192.0);
     if (t < t_ts * 0.999) {
@@ -471,10 +473,16 @@ int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt) {
   }
   *ts_mt = best_mt;
   if (force == W4A16_PREFILL_TMEM_A) return W4A16_PREFILL_TMEM_A;
-  if (force == W4A16_PREFILL_SMEM_B || M <= prefill::BMH) return W4A16_PREFILL_SMEM_B;
-  const int bn = choose_prefill_bn(M, N, num_sms, 2);
-  const long long ss_tiles = static_cast<long long>((M + prefill::BM - 1) / prefill::BM) * ((N + bn - 1) / bn);
-  const double t_ss = waves(ss_tiles) * kt * 1.12 * ss_step_model(bn, 2) / ss_step_model(prefill::BN_MAX, 2);
+  if (force == W4A16_PREFILL_SMEM_B) return W4A16_PREFILL_SMEM_B;
+  double t_ss;
+  if (M <= prefill::BMH) {
+    const int bn = choose_prefill_bn(M, N, num_sms, 1);
+    t_ss = waves((N + bn - 1) / bn) * kt * 1.07;
+  } else {
+    const int bn = choose_prefill_bn(M, N, num_sms, 2);
+    const long long ss_tiles = static_cast<long long>((M + prefill::BM - 1) / prefill::BM) * ((N + bn - 1) / bn);
+    t_ss = waves(ss_tiles) * kt * 1.12 * ss_step_model(bn, 2) / ss_step_model(prefill::BN_MAX, 2);
+  }
   return t_ts < t_ss ? W4A16_PREFILL_TMEM_A : W4A16_PREFILL_SMEM_B;
 }
 
