@@ -423,6 +423,7 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
   p.y_bf16 = y_bf16;
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  if (tiles > 0x7fffffffLL) return W4A16_ERR_INVALID;   // the kernels index tiles with int
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
   const dim3 blk(prefill::THREADS);
   if (swiglu && nat)
@@ -530,6 +531,7 @@ int launch_prefill_ts(const DeviceState& dev, const __half* x, const int32_t* qw
   p.idesc = umma_idesc_f16_f32(128, static_cast<uint32_t>(mt));
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  if (tiles > 0x7fffffffLL) return W4A16_ERR_INVALID;   // the kernels index tiles with int
   const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
   const dim3 blk(prefill_ts::THREADS);
   if (swiglu && nat)
