@@ -65,12 +65,15 @@ const char* w4a16_strerror(int status);
  *
  * workspace: device scratch of at least w4a16_gemm_workspace_size() bytes,
  * 256-byte aligned, ZEROED before its first use. The decode kernel passes the
- * partial sums of column strips shared by two or more CTAs through it (tagged
- * 64-bit words) and leaves it zero again when it completes, so one zeroed
+ * partial sums of column strips shared by two or more CTAs through its first
+ * W4A16_NOALLOC_SCRATCH_BYTES (tagged 64-bit words) and leaves them zero again;
+ * the tensor-memory-operand prefill kernel, when it splits K, keeps arrival
+ * counters (left zero) and fp32 partial tiles past that offset. So one zeroed
  * buffer serves every later call on the same stream, whatever the shape;
- * launches that may run concurrently need separate workspaces. (A launch
- * abandoned on W4A16_ERR_TIMEOUT can leave words set: zero the buffer again
- * before reusing it.) May be NULL when the size query returned 0.
+ * launches that may run concurrently need separate workspaces. A prefill call
+ * given less workspace than the query returned runs without splitting K. (A
+ * launch abandoned on W4A16_ERR_TIMEOUT can leave words set: zero the buffer
+ * again before reusing it.) May be NULL when the size query returned 0.
  */
 int w4a16_gemm(const void* x, const int32_t* qweight, const void* scales,
                const void* zeros, const void* bias, void* y,
@@ -202,8 +205,11 @@ int w4a16_gemm_host(const void* x_host, const int32_t* qweight, const void* scal
 
 /*
  * Bytes of workspace w4a16_gemm needs for this shape on the current device
- * (0 for shapes whose kernels need none). No reference counterpart: the
- * reference's kernels never split K across thread blocks.
+ * (0 for shapes whose kernels need none: N % 8 != 0, or a prefill shape run
+ * without splitting K). Shapes that route to the decode or prefill kernels need
+ * the device (its SM count); on a machine without one the query returns
+ * W4A16_ERR_DEVICE. No reference counterpart: the reference's kernels never
+ * split K across thread blocks.
  */
 int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_size,
                               int64_t* bytes_out);

@@ -38,9 +38,11 @@ def test_workspace_size_query_without_a_device():
     out = ctypes.c_int64(-1)
     lib = _lib.lib()
     assert lib.w4a16_gemm_workspace_size(1, 64, 100, 64, ctypes.byref(out)) == -1
-    # routes that need no workspace answer without touching a device
-    assert lib.w4a16_gemm_workspace_size(64, 256, 256, 64, ctypes.byref(out)) == 0 and out.value == 0
+    # the plain-load route (N % 8 != 0) needs no workspace and answers without a device;
+    # the decode and prefill routes size theirs from the device's SM count
     assert lib.w4a16_gemm_workspace_size(4, 13, 256, 64, ctypes.byref(out)) == 0 and out.value == 0
+    assert lib.w4a16_gemm_workspace_size(64, 13, 256, 64, ctypes.byref(out)) == 0 and out.value == 0
+    assert lib.w4a16_gemm_workspace_size(64, 256, 256, 64, ctypes.byref(out)) == -4   # W4A16_ERR_DEVICE
 
 
 def test_strerror_covers_every_status():

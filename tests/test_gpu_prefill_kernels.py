@@ -137,3 +137,67 @@ def test_prefill_choice_query():
             assert _lib.prefill_choice(4096, 14336, 4096) == which
     finally:
         _lib.set_prefill_kernel(_lib.PREFILL_AUTO)
+
+
+# ----------------------------------------------------------------- K split across CTAs
+# Few tiles (one row of 256-column tiles) and a long K: the TMEM-operand kernel splits K
+# over 2-4 CTAs per tile; the last split to arrive sums the fp32 partials in split order.
+SPLIT_SHAPES = [(40, 4096, 1024, 128), (100, 8192, 2048, 128), (64, 2048, 512, 64), (200, 4096, 768, 128)]
+
+
+@pytest.mark.parametrize("M,K,N,G", SPLIT_SHAPES)
+def test_split_k_matches_oracle_and_repeats(M, K, N, G):
+    X, qw, s, z = _build(M, K, N, G, sigma=0.05, seed=M + K)
+    _lib.set_prefill_kernel(_lib.PREFILL_TMEM_A)
+    try:
+        y1 = w4a16_matmul(X, qw, s, z, G)
+        y2 = w4a16_matmul(X, qw, s, z, G)
+        bias = (torch.randn(N, device="cuda") * 0.5).half()
+        yb = w4a16_matmul(X, qw, s, z, G, bias=bias)
+        f32 = w4a16.w4a16_matmul_f32(X, qw, s, z, G)
+        h = w4a16.w4a16_matmul_swiglu(X, qw, s, z, G)
+        yk = w4a16_matmul(X, w4a16.repack_qweight(qw), s, z, G, kernel_order=True)
+    finally:
+        _lib.set_prefill_kernel(_lib.PREFILL_AUTO)
+    assert _lib.check_device_errors() == 0
+    assert torch.equal(y1, y2), "split-K sums must not depend on which split arrives last"
+    assert torch.equal(y1, f32.half())
+    assert torch.equal(yb, (y1.float() + bias.float()).half())
+    assert torch.equal(yk, y1)
+    v = y1.view(M, N // 32, 2, 16)
+    plain = torch.cat([v[:, :, 0, :].reshape(M, N // 2), v[:, :, 1, :].reshape(M, N // 2)], dim=1).contiguous()
+    assert torch.equal(h, w4a16.swiglu(plain))
+    assert_gemm_close(np_(y1), oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G), f"split M={M} K={K}")
+
+
+def test_split_k_without_room_runs_unsplit():
+    """A call given no (or too little) workspace, and the allocation-free entry point
+    (whose static array leaves no room past the decode region), run without splitting K
+    and still meet the tolerance."""
+    import ctypes
+    M, K, N, G = 40, 4096, 1024, 128
+    X, qw, s, z = _build(M, K, N, G, sigma=0.05, seed=5)
+    ref = oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.set_prefill_kernel(_lib.PREFILL_TMEM_A)
+    try:
+        need = ctypes.c_int64(0)
+        assert lib.w4a16_gemm_workspace_size(M, N, K, G, ctypes.byref(need)) == 0
+        assert need.value > 5 * 1024 * 1024, "this shape is expected to split K"
+        y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+        ptrs = (X.data_ptr(), qw.data_ptr(), s.data_ptr(), z.data_ptr())
+        assert lib.w4a16_gemm(*ptrs, None, y.data_ptr(), M, N, K, G, N, None, 0, stream) == 0
+        torch.cuda.synchronize()
+        assert_gemm_close(np_(y), ref, "no workspace")
+        small = torch.zeros(need.value // 2, dtype=torch.uint8, device="cuda")
+        assert lib.w4a16_gemm(*ptrs, None, y.data_ptr(), M, N, K, G, N, small.data_ptr(), small.numel(),
+                              stream) == 0
+        torch.cuda.synchronize()
+        assert_gemm_close(np_(y), ref, "small workspace")
+        assert lib.w4a16_gemm_noalloc(*ptrs, None, y.data_ptr(), M, N, K, G, N, stream) == 0
+        torch.cuda.synchronize()
+        assert_gemm_close(np_(y), ref, "allocation-free")
+    finally:
+        _lib.set_prefill_kernel(_lib.PREFILL_AUTO)
+    assert _lib.check_device_errors() == 0

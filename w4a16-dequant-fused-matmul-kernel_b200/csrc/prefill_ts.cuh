@@ -95,7 +95,18 @@ struct Params {
   int xstages;             // x stages (X_RING_BYTES / (mt * 128), <= TST_MAX)
   uint32_t idesc;          // M=128, N=mt
   unsigned long long wait_ns;
+  int splits;              // K splits per tile (1: no split); work item = tile * splits + split
+  float* partial;          // splits > 1: fp32 partial tiles [item][epilogue warp][32 columns][mt]
+  unsigned int* counters;  // splits > 1: [tile][epilogue warp] arrivals, left zero
 };
+
+// Work item -> tile and its K-step range [k0, k1) (K split evenly into p.splits parts).
+__device__ __forceinline__ void item_range(const Params& p, int item, int KT, int& tile, int& k0, int& k1) {
+  tile = item / p.splits;
+  const int s = item - tile * p.splits;
+  k0 = static_cast<int>(static_cast<long long>(KT) * s / p.splits);
+  k1 = static_cast<int>(static_cast<long long>(KT) * (s + 1) / p.splits);
+}
 
 // SWIGLU: the weight columns are gate and up interleaved in blocks of 16, so a warp's
 // 32 lanes hold 16 gate and the matching 16 up columns; y = h [M, N/2] (plain stores).
@@ -128,7 +139,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int KT = p.K / BK;
-  const int ntiles = p.m_tiles * p.n_tiles;
+  const int nitems = p.m_tiles * p.n_tiles * p.splits;
   const int mt = p.mt;
 
   if (threadIdx.x == 0) {
@@ -167,10 +178,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       Ring r;
       long long issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-        int mi, ni;
+      for (int item = blockIdx.x; ok && item < nitems; item += gridDim.x) {
+        int tile, k0, k1, mi, ni;
+        item_range(p, item, KT, tile, k0, k1);
         prefill::tile_coords_mn(p.m_tiles, p.n_tiles, tile, mi, ni);
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = k0; kt < k1; ++kt) {
           if (!mbar_wait_backoff(&tempty[r.slot], r.phase ^ 1u, p.wait_ns, prefill::kRunAheadSleepNs)) { ok = false; break; }
           uint8_t* st = xring + r.slot * (mt * BK * 2);
           mbar_arrive_expect_tx(&tfull[r.slot], static_cast<uint32_t>(mt * BK * 2));   // the x box is [mt x 64]
@@ -191,12 +203,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       Ring t, a, d;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+      for (int item = blockIdx.x; ok && item < nitems; item += gridDim.x) {
+        int tile, k0, k1;
+        item_range(p, item, KT, tile, k0, k1);
         // this accumulator set must have been drained by the epilogue
         if (!mbar_wait(&accempty[d.slot], d.phase ^ 1u, p.wait_ns)) { ok = false; break; }
         tc_fence_after();
         const uint32_t dcol = tmem_base + static_cast<uint32_t>(d.slot * 2 * mt);
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = k0; kt < k1; ++kt) {
           // afull also implies this step's x tile has landed (the first dequantiser warp
           // waits for it before arriving): one wait per step on this thread's path
           if (!mbar_wait(&afull[a.slot], a.phase, p.wait_ns)) {
@@ -208,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t acol = tmem_base + static_cast<uint32_t>(p.a_col0 + a.slot * 64);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint32_t acc = (kt | kk) != 0 ? 1u : 0u;
+            const uint32_t acc = (kt != k0 || kk != 0) ? 1u : 0u;
             // K=16: 8 TMEM columns of A, 32 bytes along the swizzled x rows
             tc_mma_f16_ts(dcol, acol + kk * 8, bdesc + static_cast<uint64_t>(kk * 2), p.idesc, acc);
             tc_mma_f16_ts(dcol + mt, acol + 32 + kk * 8, bdesc + static_cast<uint64_t>(kk * 2), p.idesc, acc);
@@ -232,10 +246,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       Ring r;
       long long issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-        int mi, ni;
+      for (int item = blockIdx.x; ok && item < nitems; item += gridDim.x) {
+        int tile, k0, k1, mi, ni;
+        item_range(p, item, KT, tile, k0, k1);
         prefill::tile_coords_mn(p.m_tiles, p.n_tiles, tile, mi, ni);
-        for (int kt = 0; kt < KT; ++kt) {
+        for (int kt = k0; kt < k1; ++kt) {
           if (!mbar_wait_backoff(&wempty[r.slot], r.phase ^ 1u, p.wait_ns, prefill::kRunAheadSleepNs)) { ok = false; break; }
           uint8_t* st = wring + r.slot * W_BYTES;
           const int kk = kt * BK;
@@ -265,8 +280,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     Ring wr, ar, xr;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-      for (int kt = 0; kt < KT; ++kt) {
+    for (int item = blockIdx.x; ok && item < nitems; item += gridDim.x) {
+      int tile, k0, k1;
+      item_range(p, item, KT, tile, k0, k1);
+      for (int kt = k0; kt < k1; ++kt) {
         if (!warp_wait(&wfull[wr.slot], wr.phase, p.wait_ns, prefill::kRunAheadSleepNs)) {
           ok = false;
           break;
@@ -336,7 +353,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint64_t y_policy = l2_evict_first();
     if (p.tma_store && lane == 0) tma_prefetch_desc(&tm_y);
     Ring d;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+      int tile, k0, k1;
+      item_range(p, item, KT, tile, k0, k1);
       if (!warp_wait(&accfull[d.slot], d.phase, p.wait_ns, prefill::kEpilogueSleepNs)) break;
       tc_fence_after();
       int mi, ni;
@@ -350,11 +369,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         bv = p.y_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n])
                       : __half2float(static_cast<const __half*>(p.bias)[n]);
       const uint32_t dcol = tmem_base + lane_addr + static_cast<uint32_t>((d.slot * 2 + h) * mt);
-#pragma unroll 1
-      for (int mc = 0; mc < mt; mc += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(dcol + mc, r);   // r[i] = y[m0 + mc + i][n]
-        tmem_ld_wait();
+      // One 32-token chunk of the warp's 32 columns (r[i] = fp32 y[m0 + mc + i][n]): round,
+      // add the bias or apply SwiGLU, and store.
+      auto emit_chunk = [&](uint32_t (&r)[32], int mc) {
         if constexpr (SWIGLU) {
           // lanes l and l + 16 hold the gate and up values of output column ncol0 / 2 + l;
           // lane l finishes tokens 0..15 of the chunk, lane l + 16 tokens 16..31
@@ -369,7 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int m = m0 + mc + j + (up_lane ? 16 : 0);
             if (m < p.M && 2 * no < p.N) ycol[static_cast<long long>(m) * p.ldy] = swiglu_h(g, u);
           }
-          continue;
+          return;
         }
         if (p.tma_store) {
           uint8_t* sb = p.y_f32 ? stg : stg + half_sel * (STG_BYTES / 2);
@@ -413,13 +430,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_store_2d_hint(&tm_y, sb, ncol0, m0 + mc, y_policy);
             bulk_commit_group();
           }
-          continue;
+          return;
         }
         if (n < p.N) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int m = m0 + mc + i;
-            if (m >= p.M) continue;
+            if (m >= p.M) return;
             const float v = __uint_as_float(r[i]);
             if (p.y_f32) {
               static_cast<float*>(p.y)[static_cast<long long>(m) * p.ldy + n] = v;
@@ -434,6 +451,67 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
+      };
+      if (p.splits > 1) {
+        // This split's fp32 partial of the warp's 32 columns x mt tokens, then TMEM is free.
+        float* mine = p.partial + ((static_cast<long long>(item) * EPI_WARPS + e) * 32 + lane) * mt;
+#pragma unroll 1
+        for (int mc = 0; mc < mt; mc += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(dcol + mc, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<uint4*>(mine + mc + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&accempty[d.slot]);
+        d.advance(p.dsets);
+        // The split that arrives last for this warp's slice of the tile sums every split's
+        // partial in split order (one summation order whoever arrives last) and stores y.
+        __threadfence();
+        __syncwarp();
+        unsigned int* ctr = p.counters + static_cast<long long>(tile) * EPI_WARPS + e;
+        unsigned last = 0;
+        if (lane == 0) last = atomicAdd(ctr, 1u) == static_cast<unsigned>(p.splits - 1) ? 1u : 0u;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        const float* part0 = p.partial + ((static_cast<long long>(tile) * p.splits * EPI_WARPS + e) * 32 + lane) * mt;
+        const long long sstride = static_cast<long long>(EPI_WARPS) * 32 * mt;
+#pragma unroll 1
+        for (int mc = 0; mc < mt; mc += 32) {
+          uint32_t r[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(part0 + mc + i));
+            r[i] = v.x; r[i + 1] = v.y; r[i + 2] = v.z; r[i + 3] = v.w;
+          }
+#pragma unroll 1
+          for (int sp = 1; sp < p.splits; ++sp) {
+            const float* src = part0 + sp * sstride + mc;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(src + i));
+              r[i] = __float_as_uint(__uint_as_float(r[i]) + v.x);
+              r[i + 1] = __float_as_uint(__uint_as_float(r[i + 1]) + v.y);
+              r[i + 2] = __float_as_uint(__uint_as_float(r[i + 2]) + v.z);
+              r[i + 3] = __float_as_uint(__uint_as_float(r[i + 3]) + v.w);
+            }
+          }
+          emit_chunk(r, mc);
+        }
+        __syncwarp();
+        if (lane == 0) *ctr = 0u;   // left zero for the next launch
+        continue;
+      }
+#pragma unroll 1
+      for (int mc = 0; mc < mt; mc += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(dcol + mc, r);   // r[i] = y[m0 + mc + i][n]
+        tmem_ld_wait();
+        emit_chunk(r, mc);
       }
       tc_fence_before();
       __syncwarp();

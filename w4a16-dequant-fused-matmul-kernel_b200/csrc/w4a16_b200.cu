@@ -458,21 +458,43 @@ double ss_step_model(int bn, int halves) {
   return std::max(2.0 * halves * bn, (prefill::A_BYTES / 2 * halves + 36.0 * bn) / 31.5);
 }
 
-int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt) {
+// The TMEM-operand kernel's split-K area starts at byte W4A16_NOALLOC_SCRATCH_BYTES of
+// the workspace, past the decode kernel's piece words (one workspace serves every shape):
+// a fixed region of arrival counters (left zero, and never overlapped by partials of any
+// shape), then the fp32 partial tiles.
+constexpr long long kSplitCounterBytes = 64 * 1024;   // 16384 counters = 2048 tiles of 8 slices
+long long ts_split_bytes(int M, int N, int mt, int splits) {
+  if (splits <= 1) return 0;
+  const long long tiles = static_cast<long long>((M + mt - 1) / mt) * ((N + prefill_ts::NT - 1) / prefill_ts::NT);
+  return kSplitCounterBytes + tiles * splits * prefill_ts::EPI_WARPS * 32LL * mt * 4;
+}
+
+int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt, int* ts_splits = nullptr) {
   const int force = g_prefill_kernel.load(std::memory_order_relaxed);
-  const double kt = K / static_cast<double>(prefill::BK);
+  const int KT = K / prefill::BK;
+  const double kt = KT;
   auto waves = [num_sms](long long tiles) { return static_cast<double>((tiles + num_sms - 1) / num_sms); };
-  int best_mt = prefill_ts::MT_MAX;
+  int best_mt = prefill_ts::MT_MAX, best_splits = 1;
   double t_ts = 1e300;
   for (int mt = prefill_ts::MT_MAX; mt >= prefill_ts::MT_MIN; mt -= 32) {
     const long long tiles = static_cast<long long>((M + mt - 1) / mt) * ((N + prefill_ts::NT - 1) / prefill_ts::NT);
-    const double t = waves(tiles) * kt * 0.82 * (0.7 + 0.3 * mt / 192.0);
-    if (t < t_ts * 0.999) {
-      t_ts = t;
-      best_mt = mt;
+    const double step = 0.82 * (0.7 + 0.3 * mt / 192.0);
+    // K split into `sp` parts (at least 8 steps each) when the tiles do not fill one wave
+    // of CTAs: each split writes a fp32 partial tile and the last one reads them all back,
+    // and every split restarts the pipeline; ~0.07 us x mt x (1 + sp), fitted on B200 to
+    // K=4096, N=14336 (M=64: 56 -> 48 us with 2 splits; M=128: 56 -> 61 us, so kept whole).
+    const bool may_split = tiles < num_sms && tiles * prefill_ts::EPI_WARPS * 4 <= kSplitCounterBytes;
+    for (int sp = 1; sp <= 4 && (sp == 1 || (may_split && KT / sp >= 8)); ++sp) {
+      const double t = waves(tiles * sp) * ((KT + sp - 1) / sp) * step + (sp > 1 ? 0.07 * mt * (1 + sp) : 0.0);
+      if (t < t_ts * 0.97) {
+        t_ts = t;
+        best_mt = mt;
+        best_splits = sp;
+      }
     }
   }
   *ts_mt = best_mt;
+  if (ts_splits != nullptr) *ts_splits = best_splits;
   if (force == W4A16_PREFILL_TMEM_A) return W4A16_PREFILL_TMEM_A;
   if (force == W4A16_PREFILL_SMEM_B) return W4A16_PREFILL_SMEM_B;
   double t_ss;
@@ -489,7 +511,8 @@ int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt) {
 
 int launch_prefill_ts(const DeviceState& dev, const __half* x, const int32_t* qw, const __half* s,
                       const __half* z, const __half* bias, void* y, int y_f32, int M, int N, int K, int G,
-                      long long ldy, cudaStream_t stream, int swiglu, int nat, int y_bf16, int mt) {
+                      long long ldy, cudaStream_t stream, int swiglu, int nat, int y_bf16, int mt, int splits,
+                      void* workspace, int64_t workspace_bytes) {
   CUtensorMap tx, ty, tw, tsc, tz;
   if (!make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, M, K, prefill_ts::BK,
                    static_cast<uint32_t>(mt), CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -531,8 +554,22 @@ int launch_prefill_ts(const DeviceState& dev, const __half* x, const int32_t* qw
   p.idesc = umma_idesc_f16_f32(128, static_cast<uint32_t>(mt));
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
-  if (tiles > 0x7fffffffLL) return W4A16_ERR_INVALID;   // the kernels index tiles with int
-  const int grid = static_cast<int>(tiles < dev.num_sms ? tiles : dev.num_sms);
+  // split K only with room for the split area past the decode region of the workspace
+  const long long need = W4A16_NOALLOC_SCRATCH_BYTES + ts_split_bytes(M, N, mt, splits);
+  if (splits > 1 && (workspace == nullptr || workspace_bytes < need ||
+                     (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0))
+    splits = 1;
+  p.splits = splits;
+  p.counters = nullptr;
+  p.partial = nullptr;
+  if (splits > 1) {
+    uint8_t* area = static_cast<uint8_t*>(workspace) + W4A16_NOALLOC_SCRATCH_BYTES;
+    p.counters = reinterpret_cast<unsigned int*>(area);
+    p.partial = reinterpret_cast<float*>(area + kSplitCounterBytes);
+  }
+  const long long items = tiles * splits;
+  if (items > 0x7fffffffLL) return W4A16_ERR_INVALID;   // the kernels index work items with int
+  const int grid = static_cast<int>(items < dev.num_sms ? items : dev.num_sms);
   const dim3 blk(prefill_ts::THREADS);
   if (swiglu && nat)
     prefill_ts::w4a16_ts_kernel<true, true><<<grid, blk, prefill_ts::SMEM_BYTES, stream>>>(tx, ty, tw, tsc, tz, p);
@@ -655,8 +692,21 @@ int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_siz
   *bytes_out = 0;
   if (M < 0 || N < 0 || K <= 0 || group_size <= 0) return W4A16_ERR_INVALID;
   if (K % 8 != 0 || K % group_size != 0 || group_size % 64 != 0) return W4A16_ERR_INVALID;
-  if (M == 0 || N == 0 || M > 32 || N % 8 != 0 || (N + decode::BN - 1) / decode::BN > decode::MAX_STRIPS)
-    return W4A16_OK;   // routes without workspace
+  if (M == 0 || N == 0 || N % 8 != 0) return W4A16_OK;   // routes without workspace
+  if (M > 32) {
+    // the TMEM-operand prefill kernel's K splits (none: no workspace)
+    if (M > 0x7fffffffLL || N > (1ll << 30) || K > (1ll << 30)) return W4A16_ERR_INVALID;
+    DeviceState* dev = nullptr;
+    int st = current_device_state(&dev);
+    if (st != W4A16_OK) return st;
+    int mt = 0, splits = 1;
+    if (choose_prefill_kernel(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), dev->num_sms, &mt,
+                              &splits) == W4A16_PREFILL_TMEM_A && splits > 1)
+      *bytes_out = W4A16_NOALLOC_SCRATCH_BYTES +
+                   ts_split_bytes(static_cast<int>(M), static_cast<int>(N), mt, splits);
+    return W4A16_OK;
+  }
+  if ((N + decode::BN - 1) / decode::BN > decode::MAX_STRIPS) return W4A16_OK;
   DeviceState* dev = nullptr;
   int st = current_device_state(&dev);
   if (st != W4A16_OK) return st;
@@ -709,10 +759,10 @@ static int gemm_impl(const void* x, const int32_t* qweight, const void* scales, 
     return launch_decode_tma(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g,
                              ldy, workspace, workspace_bytes, s, ArArgs(), swiglu, nat, y_bf16);
   }
-  int ts_mt = 0;
-  if (choose_prefill_kernel(static_cast<int>(M), n, k, dev->num_sms, &ts_mt) == W4A16_PREFILL_TMEM_A)
+  int ts_mt = 0, ts_splits = 1;
+  if (choose_prefill_kernel(static_cast<int>(M), n, k, dev->num_sms, &ts_mt, &ts_splits) == W4A16_PREFILL_TMEM_A)
     return launch_prefill_ts(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s, swiglu,
-                             nat, y_bf16, ts_mt);
+                             nat, y_bf16, ts_mt, ts_splits, workspace, workspace_bytes);
   return launch_prefill(*dev, xh, qweight, sh, zh, bh, y, y_f32, static_cast<int>(M), n, k, g, ldy, s,
                         swiglu, nat, y_bf16);
 }
@@ -1140,7 +1190,8 @@ extern "C" int w4a16_gemm_noalloc(const void* x, const int32_t* qweight, const v
   int64_t need = 0;
   int st = w4a16_gemm_workspace_size(M, N, K, group_size, &need);
   if (st != W4A16_OK) return st;
-  if (need > W4A16_NOALLOC_SCRATCH_BYTES) return W4A16_ERR_SCRATCH_LIMIT;
+  // (prefill shapes run without K splits here: their split area lies past the array)
+  if (M <= 32 && need > W4A16_NOALLOC_SCRATCH_BYTES) return W4A16_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   st = noalloc_scratch(static_cast<cudaStream_t>(stream), &scratch);
   if (st != W4A16_OK) return st;
