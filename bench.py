@@ -15,7 +15,8 @@ One JSON line (rank 0). ``value`` is:
   Y columns) / the slowest rank's time.
 
 Extra keys carry every other configuration of the benchmark list: ``sweep``
-(M in {1,4,8,16,32} at K=8192, N=28672/p, at every N), ``gather`` (N > 1: the
+(M in {1,4,8,16,32} at K=8192, N=28672/p, at every N; ``mid_m`` adds M in {48, 96} at N = 1),
+``gather`` (N > 1: the
 same GEMM with the full Y on every rank, through the fused GEMM + all-gather
 kernel and through GEMM + NCCL all-gather), ``mlp_stack`` (80 decoder MLP blocks,
 gate/up column-parallel with SwiGLU fused into its epilogue, down row-parallel with
@@ -847,6 +848,18 @@ def run_ours(args):
         if world > 1:
             extra["gather"], good = measure_gather(ctx, args, sw, X_by_M)
             all_ok &= good
+        else:
+            # past the decode route: 48 and 96 tokens on the same weights (prefill kernels;
+            # not a BASELINE configuration, reported for the 33-128-token range)
+            from w4a16 import _lib
+            X_mid = {m: torch.randn(m, c["K"], generator=gx, device=dev).half() for m in (48, 96)}
+            y_mid = {m: torch.empty(m, sw.n, device=dev, dtype=torch.float16) for m in X_mid}
+            extra["mid_m"], good = measure_sweep(ctx, args, sw, X_mid, y_mid)
+            for e in extra["mid_m"]:
+                which = _lib.prefill_choice(e["M"], sw.n, c["K"])
+                e["roofline_per_gpu"]["kernel"] = PREFILL_KERNELS.get(which, "prefill")
+            all_ok &= good
+            del X_mid, y_mid
         del sw, X_by_M, ys
         torch.cuda.empty_cache()
     if not args.no_mlp:
