@@ -40,6 +40,12 @@
 // 4 * mt + 128 <= 512 so that the epilogue of a tile overlaps the next tile's MMAs),
 // then the A stages: stage a, half h at a_col0 + 64a + 32h (32 columns = 64 K of fp16).
 //
+// Split K: with few tiles (they do not fill one wave of CTAs) the host may split each
+// tile's K loop over 2-4 CTAs (work item = tile * splits + split). Each split's epilogue
+// writes its fp32 partial tile to the workspace and takes an arrival ticket per (tile,
+// epilogue warp); the last split sums every split's partial in split order (the bits do
+// not depend on which split arrives last), applies the output form and resets the ticket.
+//
 // Every mbarrier wait is bounded; on expiry the role raises the sticky device error
 // bit and leaves its loops; the producer drains its copies, the MMA issuer waits for
 // its MMAs, and TMEM is freed before exit.
