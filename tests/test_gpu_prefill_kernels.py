@@ -120,6 +120,31 @@ def test_prefill_kernels_agree_at_size():
     assert _lib.check_device_errors() == 0
 
 
+@pytest.mark.parametrize("M,N", [(4096, 14336), (4160, 14144), (4128, 4160)])
+def test_prefill_partial_last_tiles_at_size(kernel, M, N):
+    """Token and column counts that leave the last tiles partly empty (M = 4096 leaves 64
+    of a 192-token tile; 4160 leaves 64 rows of a 256-row tile; N = 14144 and 4160 leave
+    part of the last column tile), at a size that keeps every SM busy, so that the
+    epilogue's TMA stores are still reading their staging buffers when the chunks past M
+    or N come up: those chunks must leave the buffers alone. Repeated launches, checked
+    on the device against the fp32 torch reference with the GEMM tolerance."""
+    from tolerance import ATOL, RTOL
+    K, G = 4096, 128
+    X, qw, s, z = _build(M, K, N, G, sigma=0.02, seed=M + N)
+    ref = torch_reference(X, qw, s, z, G).float()
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    for rep in range(3):
+        y.fill_(float("nan"))
+        w4a16_matmul(X, qw, s, z, G, out=y)
+        bad = ~((y.float() - ref).abs() <= ATOL + RTOL * ref.abs())
+        if bool(bad.any()):
+            rows, cols = torch.nonzero(bad, as_tuple=True)
+            raise AssertionError(f"{kernel} M={M} N={N} launch {rep}: {int(bad.sum())} elements outside the "
+                                 f"tolerance, rows {int(rows.min())}..{int(rows.max())}, "
+                                 f"columns {int(cols.min())}..{int(cols.max())}")
+    assert _lib.check_device_errors() == 0
+
+
 def test_prefill_kernel_selection_rejects_unknown():
     with pytest.raises(RuntimeError):
         _lib.set_prefill_kernel(7)

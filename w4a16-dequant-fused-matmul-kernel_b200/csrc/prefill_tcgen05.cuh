@@ -363,6 +363,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (p.tma_store) {
           // Stage the warp's 32 x 32 chunk (row = lane) in the TMA swizzle layout and
           // store it with one bulk tensor copy; rows >= M and columns >= N are clipped.
+          // A chunk with no row below M or no column below N is neither staged nor
+          // stored: a buffer is reused after waiting for all but the latest store group,
+          // which holds only while every staged chunk commits a store.
+          if (mrow0 >= p.M || n0 + col >= p.N) continue;
           uint8_t* sb = p.y_f32 ? stg : stg + half_sel * (STG_BYTES / 2);
           if (lane == 0) {
             // the chunk that last used this buffer has left it
@@ -395,7 +399,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0 && mrow0 < p.M && n0 + col < p.N) {
+          if (lane == 0) {
             tma_store_2d_hint(&tm_y, sb, n0 + col, mrow0, y_policy);
             bulk_commit_group();
           }

@@ -378,6 +378,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       // One 32-token chunk of the warp's 32 columns (r[i] = fp32 y[m0 + mc + i][n]): round,
       // add the bias or apply SwiGLU, and store.
       auto emit_chunk = [&](uint32_t (&r)[32], int mc) {
+        // A chunk with no token below M or no column below N has nothing to store, and it
+        // must not touch the staging buffers either: the TMA-store path reuses a buffer
+        // after waiting for all but the latest store group, which holds only while every
+        // staged chunk commits a store.
+        if (m0 + mc >= p.M || ncol0 >= p.N) return;
         if constexpr (SWIGLU) {
           // lanes l and l + 16 hold the gate and up values of output column ncol0 / 2 + l;
           // lane l finishes tokens 0..15 of the chunk, lane l + 16 tokens 16..31
@@ -432,7 +437,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0 && m0 + mc < p.M && ncol0 < p.N) {
+          if (lane == 0) {
             tma_store_2d_hint(&tm_y, sb, ncol0, m0 + mc, y_policy);
             bulk_commit_group();
           }
