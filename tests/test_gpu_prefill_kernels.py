@@ -166,13 +166,15 @@ def test_prefill_choice_query():
 
 # ----------------------------------------------------------------- K split across CTAs
 # Few tiles (one row of 256-column tiles) and a long K: the TMEM-operand kernel splits K
-# over 2-4 CTAs per tile; the last split to arrive sums the fp32 partials in split order.
+# over several CTAs per tile; the last split to arrive sums the fp32 partials in split order.
 SPLIT_SHAPES = [(40, 4096, 1024, 128), (100, 8192, 2048, 128), (64, 2048, 512, 64), (200, 4096, 768, 128)]
 
 
-@pytest.mark.parametrize("M,K,N,G", SPLIT_SHAPES)
-def test_split_k_matches_oracle_and_repeats(M, K, N, G):
-    X, qw, s, z = _build(M, K, N, G, sigma=0.05, seed=M + K)
+def _check_split_case(M, K, N, G, seed):
+    """The TMEM-operand kernel forced, on a shape it runs with K splits: identical bits on
+    repeated calls, the fp32 sums, bias, SwiGLU and kernel-order forms agree with the plain
+    output; returns (X, qw, s, z, y)."""
+    X, qw, s, z = _build(M, K, N, G, sigma=0.05, seed=seed)
     _lib.set_prefill_kernel(_lib.PREFILL_TMEM_A)
     try:
         y1 = w4a16_matmul(X, qw, s, z, G)
@@ -192,7 +194,33 @@ def test_split_k_matches_oracle_and_repeats(M, K, N, G):
     v = y1.view(M, N // 32, 2, 16)
     plain = torch.cat([v[:, :, 0, :].reshape(M, N // 2), v[:, :, 1, :].reshape(M, N // 2)], dim=1).contiguous()
     assert torch.equal(h, w4a16.swiglu(plain))
-    assert_gemm_close(np_(y1), oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G), f"split M={M} K={K}")
+    return X, qw, s, z, y1
+
+
+@pytest.mark.parametrize("M,K,N,G", SPLIT_SHAPES)
+def test_split_k_matches_oracle_and_repeats(M, K, N, G):
+    X, qw, s, z, y = _check_split_case(M, K, N, G, seed=M + K)
+    assert_gemm_close(np_(y), oracle.reference_w4a16(np_(X), np_(qw), np_(s), np_(z), G), f"split M={M} K={K}")
+
+
+# More tiles than CTAs with the last wave partly filled (tiles mod 148 = 2, 44, 64 at 128, 160
+# and 192 tokens per tile): the tiles of the full waves run whole, the last wave's tiles are
+# split into 2-3 parts whose partials the last split to arrive sums.
+TAIL_SHAPES = [(200, 4096, 19200, 128), (300, 4096, 24576, 128), (500, 4096, 30720, 128)]
+
+
+@pytest.mark.parametrize("M,K,N,G", TAIL_SHAPES)
+def test_tail_split_matches_reference_and_repeats(M, K, N, G):
+    import ctypes
+    need = ctypes.c_int64(0)
+    _lib.set_prefill_kernel(_lib.PREFILL_TMEM_A)
+    try:
+        assert _lib.lib().w4a16_gemm_workspace_size(M, N, K, G, ctypes.byref(need)) == 0
+    finally:
+        _lib.set_prefill_kernel(_lib.PREFILL_AUTO)
+    assert need.value > 5 * 1024 * 1024, "this shape is expected to split the last wave's tiles"
+    X, qw, s, z, y = _check_split_case(M, K, N, G, seed=M + N)
+    assert_gemm_close(np_(y), np_(torch_reference(X, qw, s, z, G)), f"tail split M={M} N={N}")
 
 
 def test_split_k_without_room_runs_unsplit():

@@ -40,11 +40,13 @@
 // 4 * mt + 128 <= 512 so that the epilogue of a tile overlaps the next tile's MMAs),
 // then the A stages: stage a, half h at a_col0 + 64a + 32h (32 columns = 64 K of fp16).
 //
-// Split K: with few tiles (they do not fill one wave of CTAs) the host may split each
-// tile's K loop over 2-4 CTAs (work item = tile * splits + split). Each split's epilogue
-// writes its fp32 partial tile to the workspace and takes an arrival ticket per (tile,
-// epilogue warp); the last split sums every split's partial in split order (the bits do
-// not depend on which split arrives last), applies the output form and resets the ticket.
+// Split K: the host may split the K loop of some tiles over several CTAs: of every tile
+// when the tiles do not fill one wave of CTAs (whole = 0), or of the tiles of the last,
+// partly filled wave (whole = the tiles of the full waves, a multiple of the grid, so
+// every CTA runs the same number of whole tiles first). Each split's epilogue writes its
+// fp32 partial tile to the workspace and takes an arrival ticket per (tile, epilogue
+// warp); the last split sums every split's partial in split order (the bits do not
+// depend on which split arrives last), applies the output form and resets the ticket.
 //
 // Every mbarrier wait is bounded; on expiry the role raises the sticky device error
 // bit and leaves its loops; the producer drains its copies, the MMA issuer waits for
@@ -101,17 +103,33 @@ struct Params {
   int xstages;             // x stages (X_RING_BYTES / (mt * 128), <= TST_MAX)
   uint32_t idesc;          // M=128, N=mt
   unsigned long long wait_ns;
-  int splits;              // K splits per tile (1: no split); work item = tile * splits + split
-  float* partial;          // splits > 1: fp32 partial tiles [item][epilogue warp][32 columns][mt]
-  unsigned int* counters;  // splits > 1: [tile][epilogue warp] arrivals, left zero
+  int splits;              // K splits of each tile past `whole` (1: no split)
+  int whole;               // tiles [0, whole) run whole, one work item each; tile whole + t is
+                           // split into items whole + t * splits + s (s < splits)
+  float* partial;          // splits > 1: fp32 partial tiles [split item][epilogue warp][mt tokens][32 columns]
+  unsigned int* counters;  // splits > 1: [split tile][epilogue warp] arrivals, left zero
 };
 
-// Work item -> tile and its K-step range [k0, k1) (K split evenly into p.splits parts).
-__device__ __forceinline__ void item_range(const Params& p, int item, int KT, int& tile, int& k0, int& k1) {
-  tile = item / p.splits;
-  const int s = item - tile * p.splits;
+__device__ __forceinline__ int num_items(const Params& p) {
+  return p.whole + (p.m_tiles * p.n_tiles - p.whole) * p.splits;
+}
+
+// Work item -> tile and its K-step range [k0, k1) (K split evenly into p.splits parts for
+// the tiles past p.whole); true for a split item.
+__device__ __forceinline__ bool item_range(const Params& p, int item, int KT, int& tile, int& k0, int& k1) {
+  if (item < p.whole) {
+    tile = item;
+    k0 = 0;
+    k1 = KT;
+    return false;
+  }
+  const int i = item - p.whole;
+  const int t = i / p.splits;
+  const int s = i - t * p.splits;
+  tile = p.whole + t;
   k0 = static_cast<int>(static_cast<long long>(KT) * s / p.splits);
   k1 = static_cast<int>(static_cast<long long>(KT) * (s + 1) / p.splits);
+  return p.splits > 1;
 }
 
 // SWIGLU: the weight columns are gate and up interleaved in blocks of 16, so a warp's
@@ -145,7 +163,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int KT = p.K / BK;
-  const int nitems = p.m_tiles * p.n_tiles * p.splits;
+  const int nitems = num_items(p);
   const int mt = p.mt;
 
   if (threadIdx.x == 0) {
@@ -361,7 +379,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     Ring d;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
       int tile, k0, k1;
-      item_range(p, item, KT, tile, k0, k1);
+      const bool split = item_range(p, item, KT, tile, k0, k1);
       if (!warp_wait(&accfull[d.slot], d.phase, p.wait_ns, prefill::kEpilogueSleepNs)) break;
       tc_fence_after();
       int mi, ni;
@@ -463,17 +481,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       };
-      if (p.splits > 1) {
+      if (split) {
         // This split's fp32 partial of the warp's 32 columns x mt tokens, then TMEM is free.
-        float* mine = p.partial + ((static_cast<long long>(item) * EPI_WARPS + e) * 32 + lane) * mt;
+        // Token-major ([token][32 columns] per warp): the warp's store or load of one token
+        // is one 128-byte line.
+        float* mine = p.partial + (static_cast<long long>(item - p.whole) * EPI_WARPS + e) * 32LL * mt + lane;
 #pragma unroll 1
         for (int mc = 0; mc < mt; mc += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(dcol + mc, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<uint4*>(mine + mc + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+          for (int i = 0; i < 32; ++i) mine[(mc + i) * 32] = __uint_as_float(r[i]);
         }
         tc_fence_before();
         __syncwarp();
@@ -483,33 +502,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         // partial in split order (one summation order whoever arrives last) and stores y.
         __threadfence();
         __syncwarp();
-        unsigned int* ctr = p.counters + static_cast<long long>(tile) * EPI_WARPS + e;
+        unsigned int* ctr = p.counters + static_cast<long long>(tile - p.whole) * EPI_WARPS + e;
         unsigned last = 0;
         if (lane == 0) last = atomicAdd(ctr, 1u) == static_cast<unsigned>(p.splits - 1) ? 1u : 0u;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
-        const float* part0 = p.partial + ((static_cast<long long>(tile) * p.splits * EPI_WARPS + e) * 32 + lane) * mt;
+        const float* part0 =
+            p.partial + static_cast<long long>(tile - p.whole) * p.splits * EPI_WARPS * 32LL * mt + e * 32LL * mt + lane;
         const long long sstride = static_cast<long long>(EPI_WARPS) * 32 * mt;
 #pragma unroll 1
         for (int mc = 0; mc < mt; mc += 32) {
           uint32_t r[32];
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(part0 + mc + i));
-            r[i] = v.x; r[i + 1] = v.y; r[i + 2] = v.z; r[i + 3] = v.w;
-          }
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__ldcg(part0 + (mc + i) * 32));
 #pragma unroll 1
           for (int sp = 1; sp < p.splits; ++sp) {
-            const float* src = part0 + sp * sstride + mc;
+            const float* src = part0 + sp * sstride + mc * 32;
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(src + i));
-              r[i] = __float_as_uint(__uint_as_float(r[i]) + v.x);
-              r[i + 1] = __float_as_uint(__uint_as_float(r[i + 1]) + v.y);
-              r[i + 2] = __float_as_uint(__uint_as_float(r[i + 2]) + v.z);
-              r[i + 3] = __float_as_uint(__uint_as_float(r[i + 3]) + v.w);
-            }
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) + __ldcg(src + i * 32));
           }
           emit_chunk(r, mc);
         }

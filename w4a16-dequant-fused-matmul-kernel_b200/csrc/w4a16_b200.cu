@@ -463,11 +463,29 @@ double ss_step_model(int bn, int halves) {
 // a fixed region of arrival counters (left zero, and never overlapped by partials of any
 // shape), then the fp32 partial tiles.
 constexpr long long kSplitCounterBytes = 64 * 1024;   // 16384 counters = 2048 tiles of 8 slices
-long long ts_split_bytes(int M, int N, int mt, int splits) {
+
+// The tiles that run whole ahead of the split ones: none when every tile is split (the
+// tiles do not fill one wave of CTAs), else the tiles of the full waves of a grid of
+// num_sms CTAs, so that each CTA runs the same number of whole tiles and then the split
+// items of the last wave's tiles.
+long long ts_whole_tiles(long long tiles, int splits, int num_sms) {
+  if (splits <= 1) return tiles;
+  return tiles < num_sms ? 0 : tiles / num_sms * num_sms;
+}
+
+long long ts_split_bytes(int M, int N, int mt, int splits, int num_sms) {
   if (splits <= 1) return 0;
   const long long tiles = static_cast<long long>((M + mt - 1) / mt) * ((N + prefill_ts::NT - 1) / prefill_ts::NT);
-  return kSplitCounterBytes + tiles * splits * prefill_ts::EPI_WARPS * 32LL * mt * 4;
+  const long long split_tiles = tiles - ts_whole_tiles(tiles, splits, num_sms);
+  return kSplitCounterBytes + split_tiles * splits * prefill_ts::EPI_WARPS * 32LL * mt * 4;
 }
+
+// K splits of the TMEM-operand kernel: at most kMaxSplits parts of at least 8 steps. A split
+// costs its pipeline restart plus, in the last split to arrive, one L2 round trip per
+// 32-token chunk for each other split's partial: ~4 + 6.5 x sp x mt / 192 us, fitted on B200
+// (K=4096, N=14336, mt=192, M=512..8192 with 2-7 splits of the last wave's tiles).
+constexpr int kMaxSplits = 8;
+double split_cost_us(int mt, int sp) { return 4.0 + 6.5 * sp * mt / 192.0; }
 
 int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt, int* ts_splits = nullptr) {
   const int force = g_prefill_kernel.load(std::memory_order_relaxed);
@@ -479,13 +497,25 @@ int choose_prefill_kernel(int M, int N, int K, int num_sms, int* ts_mt, int* ts_
   for (int mt = prefill_ts::MT_MAX; mt >= prefill_ts::MT_MIN; mt -= 32) {
     const long long tiles = static_cast<long long>((M + mt - 1) / mt) * ((N + prefill_ts::NT - 1) / prefill_ts::NT);
     const double step = 0.82 * (0.7 + 0.3 * mt / 192.0);
-    // K split into `sp` parts (at least 8 steps each) when the tiles do not fill one wave
-    // of CTAs: each split writes a fp32 partial tile and the last one reads them all back,
-    // and every split restarts the pipeline; ~0.07 us x mt x (1 + sp), fitted on B200 to
-    // K=4096, N=14336 (M=64: 56 -> 48 us with 2 splits; M=128: 56 -> 61 us, so kept whole).
+    // K split into `sp` parts when the tiles do not fill one wave of CTAs (every tile
+    // split: each split writes a fp32 partial tile and the last one reads them all back).
     const bool may_split = tiles < num_sms && tiles * prefill_ts::EPI_WARPS * 4 <= kSplitCounterBytes;
-    for (int sp = 1; sp <= 4 && (sp == 1 || (may_split && KT / sp >= 8)); ++sp) {
-      const double t = waves(tiles * sp) * ((KT + sp - 1) / sp) * step + (sp > 1 ? 0.07 * mt * (1 + sp) : 0.0);
+    // With more tiles than CTAs, only the last, partly filled wave's tiles may be split,
+    // into as many parts as keep that wave to one pass of the grid: the full waves' time
+    // plus one split's steps plus the split's cost.
+    const long long full = tiles / num_sms * num_sms, rem = tiles - full;
+    const bool may_split_tail = full > 0 && rem > 0;
+    for (int sp = 1; sp <= kMaxSplits && (sp == 1 || KT / sp >= 8); ++sp) {
+      double t;
+      if (sp == 1) {
+        t = waves(tiles) * kt * step;
+      } else if (may_split) {
+        t = waves(tiles * sp) * ((KT + sp - 1) / sp) * step + split_cost_us(mt, sp);
+      } else if (may_split_tail && rem * sp <= num_sms) {
+        t = static_cast<double>(full / num_sms) * kt * step + ((KT + sp - 1) / sp) * step + split_cost_us(mt, sp);
+      } else {
+        break;
+      }
       if (t < t_ts * 0.97) {
         t_ts = t;
         best_mt = mt;
@@ -555,7 +585,7 @@ int launch_prefill_ts(const DeviceState& dev, const __half* x, const int32_t* qw
   p.wait_ns = g_wait_budget_ns.load(std::memory_order_relaxed);
   const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
   // split K only with room for the split area past the decode region of the workspace
-  const long long need = W4A16_NOALLOC_SCRATCH_BYTES + ts_split_bytes(M, N, mt, splits);
+  const long long need = W4A16_NOALLOC_SCRATCH_BYTES + ts_split_bytes(M, N, mt, splits, dev.num_sms);
   if (splits > 1 && (workspace == nullptr || workspace_bytes < need ||
                      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0))
     splits = 1;
@@ -567,8 +597,10 @@ int launch_prefill_ts(const DeviceState& dev, const __half* x, const int32_t* qw
     p.counters = reinterpret_cast<unsigned int*>(area);
     p.partial = reinterpret_cast<float*>(area + kSplitCounterBytes);
   }
-  const long long items = tiles * splits;
-  if (items > 0x7fffffffLL) return W4A16_ERR_INVALID;   // the kernels index work items with int
+  const long long whole = ts_whole_tiles(tiles, splits, dev.num_sms);
+  p.whole = static_cast<int>(std::min<long long>(whole, 0x7fffffffLL));
+  const long long items = whole + (tiles - whole) * splits;
+  if (items > 0x7fffffffLL || tiles > 0x7fffffffLL) return W4A16_ERR_INVALID;   // the kernels index work items with int
   const int grid = static_cast<int>(items < dev.num_sms ? items : dev.num_sms);
   const dim3 blk(prefill_ts::THREADS);
   if (swiglu && nat)
@@ -703,7 +735,7 @@ int w4a16_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t group_siz
     if (choose_prefill_kernel(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), dev->num_sms, &mt,
                               &splits) == W4A16_PREFILL_TMEM_A && splits > 1)
       *bytes_out = W4A16_NOALLOC_SCRATCH_BYTES +
-                   ts_split_bytes(static_cast<int>(M), static_cast<int>(N), mt, splits);
+                   ts_split_bytes(static_cast<int>(M), static_cast<int>(N), mt, splits, dev->num_sms);
     return W4A16_OK;
   }
   if ((N + decode::BN - 1) / decode::BN > decode::MAX_STRIPS) return W4A16_OK;
