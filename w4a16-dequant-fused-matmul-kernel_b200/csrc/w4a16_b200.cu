@@ -449,9 +449,10 @@ int launch_prefill(const DeviceState& dev, const __half* x, const int32_t* qw, c
 //   shared-memory operand kernel, single 128-row half (M <= 128): ~1.07 us per step,
 //     latency-bound (its dequantisers prefetch only two steps ahead), whatever bn.
 // The TMEM-operand tile does ~1.17x the work per unit time, so it wins unless its
-// coarser wave quantisation loses more (M = 512; N = 8192 at M = 2048). At 33-128
-// tokens it takes 56 vs 68.5 us (K=4096, N=14336) and 101-104 vs 138 us (K=8192,
-// N=28672). w4a16_set_prefill_kernel() overrides the choice (tests exercise both).
+// coarser wave quantisation loses more (N = 8192 at M = 2048), which its K splits
+// (split_cost_us) partly recover. At 33-128 tokens it takes 42-46 vs 68.5 us (K=4096,
+// N=14336) and 101-104 vs 138 us (K=8192, N=28672). w4a16_set_prefill_kernel()
+// overrides the choice (tests exercise both).
 std::atomic<int> g_prefill_kernel{W4A16_PREFILL_AUTO};
 
 double ss_step_model(int bn, int halves) {
