@@ -4,7 +4,8 @@ The numpy oracle cannot finish these in seconds, so the checks are (a) a
 plain-PyTorch fp32 reference on the GPU that restates the oracle's arithmetic
 (tests/helpers.py), (b) the oracle itself on a few rows, and (c) properties
 that hold at any size: column shards of the weight give the matching column
-slice of the output, and row slices the matching rows.
+slice of the output, and row slices the matching rows (bit for bit unless a call
+splits K across CTAs).
 """
 from __future__ import annotations
 
@@ -58,9 +59,24 @@ def test_prefill_configuration(M):
     X, W = gpu_case(M, 4096, 14336, 128, sigma=0.02, seed=4)
     qw, s, z = quantize_weight(W, 128)
     y = _check(X, qw, s, z, 128, f"prefill M={M}")
-    # row slices through the same kernel are the matching rows
-    ys = w4a16_matmul(X[M // 2:M // 2 + 256].contiguous(), qw, s, z, 128)
-    assert torch.equal(ys, y[M // 2:M // 2 + 256])
+    # row slices are the matching rows: bit for bit when neither call splits K across
+    # CTAs (the same summation order per output), within the GEMM tolerance otherwise
+    rows = slice(M // 2, M // 2 + 256)
+    ys = w4a16_matmul(X[rows].contiguous(), qw, s, z, 128)
+    if _splits_k(M, 14336, 4096) or _splits_k(256, 14336, 4096):
+        assert_gemm_close(np_(ys), np_(y[rows]).astype("float32"), f"row slice of M={M}")
+    else:
+        assert torch.equal(ys, y[rows])
+
+
+def _splits_k(M, N, K, G=128):
+    """True when the shape's prefill GEMM splits K across CTAs: the workspace it asks
+    for reaches past the decode region."""
+    import ctypes
+    from w4a16 import _lib
+    need = ctypes.c_int64(0)
+    assert _lib.lib().w4a16_gemm_workspace_size(M, N, K, G, ctypes.byref(need)) == 0
+    return need.value > 5 * 1024 * 1024
 
 
 @pytest.mark.parametrize("M", [1, 2048])
