@@ -302,6 +302,15 @@ int w4a16_set_prefill_kernel(int which);
  * M x N x K GEMM with N % 8 == 0 on the current device, or W4A16_PREFILL_AUTO when M <= 32
  * (decode). For reports and tests; no reference counterpart. */
 int w4a16_prefill_choice(int64_t M, int64_t N, int64_t K, int* which);
+/* The plan the cost model makes for an M x N x K GEMM (K % 64 == 0) on a GPU with num_sms
+ * SMs, under the current selection, without touching a device: *which as in
+ * w4a16_prefill_choice; for the tensor-memory-operand kernel *tokens_per_tile (its tile
+ * height, 64..192) and *splits (K split over that many CTAs for the tiles it splits: every
+ * tile when the tiles do not fill one wave, else the last wave's; 1: none), else 0 and 1.
+ * A launch splits K only when it is given the workspace the size query returns. For reports
+ * and tests; no reference counterpart. */
+int w4a16_prefill_plan(int64_t M, int64_t N, int64_t K, int num_sms, int* which, int* tokens_per_tile,
+                       int* splits);
 
 /*
  * After W4A16_ERR_TIMEOUT: zero `workspace_bytes` of a caller's GEMM workspace

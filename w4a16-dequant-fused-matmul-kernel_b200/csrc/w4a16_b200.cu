@@ -1115,6 +1115,24 @@ int w4a16_prefill_choice(int64_t M, int64_t N, int64_t K, int* which) {
   return W4A16_OK;
 }
 
+int w4a16_prefill_plan(int64_t M, int64_t N, int64_t K, int num_sms, int* which, int* tokens_per_tile,
+                       int* splits) {
+  if (which == nullptr || tokens_per_tile == nullptr || splits == nullptr || num_sms <= 0 || num_sms > 4096 ||
+      M <= 0 || N <= 0 || K <= 0 || K % prefill::BK != 0 || M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff)
+    return W4A16_ERR_INVALID;
+  if (M <= 32) {
+    *which = W4A16_PREFILL_AUTO;
+    *tokens_per_tile = 0;
+    *splits = 1;
+    return W4A16_OK;
+  }
+  int mt = 0, sp = 1;
+  *which = choose_prefill_kernel(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), num_sms, &mt, &sp);
+  *tokens_per_tile = *which == W4A16_PREFILL_TMEM_A ? mt : 0;
+  *splits = *which == W4A16_PREFILL_TMEM_A ? sp : 1;
+  return W4A16_OK;
+}
+
 int w4a16_set_prefill_kernel(int which) {
   if (which != W4A16_PREFILL_AUTO && which != W4A16_PREFILL_SMEM_B && which != W4A16_PREFILL_TMEM_A)
     return W4A16_ERR_INVALID;

@@ -56,6 +56,8 @@ SIGNATURES = {
     "w4a16_set_wait_budget_ns": ([_c_i64], ctypes.c_int),
     "w4a16_set_prefill_kernel": ([ctypes.c_int], ctypes.c_int),
     "w4a16_prefill_choice": ([_c_i64, _c_i64, _c_i64, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "w4a16_prefill_plan": ([_c_i64, _c_i64, _c_i64, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                            ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "w4a16_reset_scratch": ([_vp, _c_i64, _vp], ctypes.c_int),
     "w4a16_gemm_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                             _vp], ctypes.c_int),
@@ -253,3 +255,14 @@ def prefill_choice(M: int, N: int, K: int) -> int:
     which = ctypes.c_int(0)
     check(lib().w4a16_prefill_choice(int(M), int(N), int(K), ctypes.byref(which)), "w4a16_prefill_choice")
     return which.value
+
+
+def prefill_plan(M: int, N: int, K: int, num_sms: int) -> tuple[int, int, int]:
+    """(kernel, tokens per tile, K splits) the cost model picks for an M x N x K GEMM on a
+    GPU with ``num_sms`` SMs under the current selection, computed on the host (no device
+    needed): as :func:`prefill_choice` for the kernel; tokens per tile and splits describe
+    the tensor-memory-operand kernel (0 and 1 for the other kernel and for M <= 32)."""
+    which, mt, sp = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    check(lib().w4a16_prefill_plan(int(M), int(N), int(K), int(num_sms), ctypes.byref(which), ctypes.byref(mt),
+                                   ctypes.byref(sp)), "w4a16_prefill_plan")
+    return which.value, mt.value, sp.value
